@@ -1,0 +1,407 @@
+#!/usr/bin/env python3
+"""Benchmark: MXFP6 GEMM TFLOPS on B200 (BASELINE metric), one JSON line on rank 0.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config cfg2]
+
+Workload (a "step" = one D = A·B call over one batch of synthetic operands):
+  N=1   BASELINE config 2: M=N=K=8192, FP16 out, E2M3 codes uniform over all 64 codes, E8M0
+        exponents uniform in [118, 136] (seeded; no dataset).
+  N>1   the same per-GPU shape, N-sharded (column-parallel): the job is D[8192, 8192*N] =
+        A[8192, 8192] · B[8192, 8192*N] with A replicated and B / D split by columns, so per-GPU
+        work is fixed (weak scaling) and no collective sits on the GEMM path. The optional NCCL
+        all-gather of D is timed separately ("allgather").
+Other configs (--config cfg1..cfg5) run the same harness on BASELINE's other shapes.
+
+Timing: W untimed warm-up steps; then exactly K steps between a barrier + synchronize on each
+side; before every timed step a 256 MiB buffer is written to flush the 126 MB L2, and each
+step's GEMM is bracketed by CUDA events on the launching stream; ms_per_step is the mean over
+the K steps, maximised over ranks. Clocks are sampled through NVML during the timed region.
+
+--impl reference times the reference's own CPU GEMM (mxfp6_gemm_ref, compiled from its sources
+into oracle/_ref) on the host cores, on a bounded row sample of the same workload; rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "mxfp6-gemm_b200"))
+
+CONFIGS = {
+    # name: (M, N, K, kind, exp_range, out)
+    "cfg1": (256, 256, 512, "codes", (120, 134), "F32"),
+    "cfg2": (8192, 8192, 8192, "codes", (118, 136), "F16"),
+    "cfg3": (2048, 1024, 105728, "codes", (118, 136), "F16"),
+    "cfg4": (2048, 6144, 16128, "codes", (118, 136), "BF16"),
+    "cfg5": (4096, 28672, 8192, "normal", None, "BF16"),
+}
+CONFIG_DESC = {
+    "cfg1": "MXFP6 GEMM M=256 N=256 K=512, FP32 output",
+    "cfg2": "MXFP6 GEMM M=8192 N=8192 K=8192, FP16 output",
+    "cfg3": "MXFP6 GEMM M=2048 N=1024 K=105728, FP16 output, split-K",
+    "cfg4": "MXFP6 GEMM M=2048 N=6144 K=16128, BF16 output",
+    "cfg5": "LLM FFN up-projection MXFP6 GEMM M=4096 N=28672 K=8192, BF16 output",
+}
+METRIC = "MXFP6 GEMM TFLOPS (2*M*N*K / device time)"
+L2_FLUSH_BYTES = 256 << 20
+
+
+def load_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            p = json.load(f)
+        return float(p["bf16_tflops"]), float(p["hbm_gbs"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return 1590.0, 6650.0, "fallback"
+
+
+class ClockSampler:
+    """Samples SM clock and throttle reasons through NVML while running."""
+
+    REASONS = {
+        0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap", 0x8: "hw_slowdown",
+        0x10: "sync_boost", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+        0x80: "hw_power_brake_slowdown", 0x100: "display_clock_setting",
+    }
+
+    def __init__(self, index: int):
+        self.samples, self.reasons, self.max_mhz = [], 0, None
+        self._stop = threading.Event()
+        self._thread = None
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.nvml = pynvml
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+        except Exception:  # NVML missing: report no clocks rather than fail the bench
+            self.nvml = None
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                self.samples.append(self.nvml.nvmlDeviceGetClockInfo(self.h, self.nvml.NVML_CLOCK_SM))
+                self.reasons |= self.nvml.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+            except Exception:
+                pass
+            time.sleep(0.005)
+
+    def __enter__(self):
+        if self.nvml:
+            self._thread = threading.Thread(target=self._run, daemon=True)
+            self._thread.start()
+        return self
+
+    def __exit__(self, *a):
+        self._stop.set()
+        if self._thread:
+            self._thread.join()
+
+    def summary(self):
+        if not self.nvml:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvml_unavailable"], "samples": 0}
+        names = [n for b, n in self.REASONS.items() if self.reasons & b and n != "gpu_idle"]
+        return {"sm_mhz": statistics.median(self.samples) if self.samples else None,
+                "sm_max_mhz": self.max_mhz, "reasons": names, "samples": len(self.samples)}
+
+
+def dist_env():
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return rank, world, local
+
+
+# ---- reference arm: the reference's CPU GEMM on the host cores ------------------------------------
+
+def _cpu_threads(N, K):
+    """All host threads, capped so that each thread's private dequantised copy of B (the
+    reference's mxfp6_gemm_ref dequantises both operands per call) fits in available memory."""
+    threads = os.cpu_count() or 1
+    try:
+        avail = os.sysconf("SC_AVPHYS_PAGES") * os.sysconf("SC_PAGE_SIZE")
+    except (ValueError, OSError):
+        avail = 16 << 30
+    per_thread = N * K * 4 + 64 * K * 4
+    return max(1, min(threads, int(avail * 0.5 // per_thread)))
+
+
+_CPU_OPS = {}
+
+
+def cpu_reference_sample(cfg_name, target_s=10.0, threads=None, rows_override=None):
+    """Time mxfp6_gemm_ref (oracle/_ref, the reference's own CPU path; else the C restatement)
+    on a row sample of the config: `rows` rows of A against all of B, sized to about target_s."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    from oracle import Oracle, Reference, reference_available
+    from mxfp6_b200.synth import make_operands
+
+    M, N, K, kind, er, _ = CONFIGS[cfg_name]
+    threads = threads or _cpu_threads(N, K)
+    kw = {"exp_range": er} if er else {}
+    if cfg_name not in _CPU_OPS:  # same distributions as the GPU run
+        _CPU_OPS[cfg_name] = make_operands(M, N, K, kind=kind, seed=2026, **kw)
+    ops = _CPU_OPS[cfg_name]
+    if reference_available() and ops.Kp == K:
+        ref, kind_s = Reference(), "reference"
+
+        def run(rows):
+            return ref.gemm(ops.A[:rows], ops.sA[:rows], ops.Bt, ops.sB, K, threads=threads)
+    else:
+        o, kind_s = Oracle(), "port"
+
+        def run(rows):
+            return o.gemm(ops.A[:rows], ops.sA[:rows], ops.Bt, ops.sB, ops.Kp, threads=threads)
+
+    if rows_override is None:
+        probe = min(ops.M, threads)
+        t0 = time.perf_counter()
+        run(probe)
+        t_probe = time.perf_counter() - t0
+        rows = int(probe * target_s / max(t_probe, 1e-3))
+        rows = max(probe, min(ops.M, rows // threads * threads if rows >= threads else rows))
+    else:
+        rows = min(rows_override, ops.M)
+    t0 = time.perf_counter()
+    run(rows)
+    dt = time.perf_counter() - t0
+    tflops = 2.0 * rows * N * K / dt / 1e12
+    sample = (f"{rows} of {M} rows of A x all {N} columns of B, K={K} "
+              f"({2.0 * rows * N * K / 1e9:.1f} GFLOP) in {dt:.2f} s on {threads} threads")
+    return tflops, kind_s, threads, sample, rows
+
+
+def run_reference_arm(args):
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return
+    _, _, _, _, _, out = CONFIGS[args.config]
+    M, N, K = CONFIGS[args.config][:3]
+    threads = _cpu_threads(N, K)
+    # one calibration pass picks the row sample, then K timed steps of that sample
+    v0, kind_s, cores, sample, rows = cpu_reference_sample(args.config, target_s=min(args.ref_seconds, 150.0 / max(1, args.steps + args.warmup)),
+                                                           threads=threads)
+    for _ in range(max(0, min(args.warmup, 1) - 1)):
+        cpu_reference_sample(args.config, threads=threads, rows_override=rows)
+    vals = []
+    for _ in range(args.steps):
+        v, kind_s, cores, sample, _ = cpu_reference_sample(args.config, threads=threads, rows_override=rows)
+        vals.append(v)
+    value = statistics.mean(vals)
+    flops_step = 2.0 * rows * N * K
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "TFLOPS", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": flops_step / (value * 1e12) * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded E2M3 codes / E8M0 scales, BASELINE distributions)",
+        "config": {"workload": CONFIG_DESC[args.config], "M": M, "N": N, "K": K, "out": out,
+                   "sample_rows": rows},
+        "cpu_baseline": {"value": value, "unit": "TFLOPS", "cores": cores, "kind": kind_s, "sample": sample},
+        "e2e": {"value": value, "unit": "TFLOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---- our arm ----------------------------------------------------------------------------------------
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    import mxfp6_b200 as lib
+    from mxfp6_b200.synth import make_operands
+
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+
+    M, N, K, kind, er, out_name = CONFIGS[args.config]
+    ot = lib.OutType[out_name]
+    kw = {"exp_range": er} if er else {}
+    # A is replicated (same seed everywhere); B^T's shard differs per rank (column-parallel).
+    a_ops = make_operands(M, 128, K, kind=kind, seed=1000, **kw)
+    b_ops = make_operands(128, N, K, kind=kind, seed=2000 + rank, **kw)
+    Kp = a_ops.Kp
+    rb = Kp * 3 // 4
+    A = torch.from_numpy(a_ops.A).to(dev)
+    Bt = torch.from_numpy(b_ops.Bt).to(dev)
+    sA = torch.from_numpy(lib.preprocess_scale(a_ops.sA, M, Kp)).to(dev)
+    sB = torch.from_numpy(lib.preprocess_scale(b_ops.sB, N, Kp)).to(dev)
+    tdt = {lib.OutType.F32: torch.float32, lib.OutType.F16: torch.float16, lib.OutType.BF16: torch.bfloat16}[ot]
+    D = torch.empty((M, N), dtype=tdt, device=dev)
+    wsb = lib.gemm_workspace_size(M, N, Kp)
+    ws = torch.empty(max(wsb, 16), dtype=torch.uint8, device=dev)
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        lib.gemm(ot, M, N, Kp, A, Bt, sA, sB, D, rb, rb, ws if wsb else None, wsb, stream=stream)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    assert lib.last_error() == lib.OK, lib.last_error_string()
+    assert lib.device_status() == 0
+
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    launches0 = lib.launch_count()
+    with ClockSampler(local) as clk:
+        for i in range(args.steps):
+            flush.fill_(i & 0xFF)
+            starts[i].record(stream)
+            step()
+            ends[i].record(stream)
+        torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    launches = lib.launch_count() - launches0
+    status = lib.device_status()
+    per = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    ms = sum(per) / len(per)
+    if world > 1:
+        t = torch.tensor([ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    flops_rank = 2.0 * M * N * K
+    value = flops_rank * world / (ms * 1e-3) / 1e12
+
+    # ---- end to end through the C ABI with host buffers ----
+    pinned = {k: v.cpu().pin_memory() for k, v in (("A", A), ("Bt", Bt), ("sA", sA), ("sB", sB))}
+    dA2, dB2, dsA2, dsB2 = (torch.empty_like(t) for t in (A, Bt, sA, sB))
+    Dh = torch.empty((M, N), dtype=tdt).pin_memory()
+    h2d = sum(p.numel() * p.element_size() for p in pinned.values())
+    d2h = Dh.numel() * Dh.element_size()
+
+    def e2e_step():
+        dA2.copy_(pinned["A"], non_blocking=True)
+        dB2.copy_(pinned["Bt"], non_blocking=True)
+        dsA2.copy_(pinned["sA"], non_blocking=True)
+        dsB2.copy_(pinned["sB"], non_blocking=True)
+        lib.gemm(ot, M, N, Kp, dA2, dB2, dsA2, dsB2, D, rb, rb, ws if wsb else None, wsb, stream=stream)
+        Dh.copy_(D, non_blocking=True)
+
+    e2e_steps = max(3, min(args.steps, 20))
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / e2e_steps
+    if world > 1:
+        t = torch.tensor([e2e_ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    e2e_value = flops_rank * world / (e2e_ms * 1e-3) / 1e12
+
+    # ---- optional NCCL all-gather of the D shards (timed separately) ----
+    allgather = None
+    if world > 1 and not args.no_allgather:
+        gathered = torch.empty((world,) + tuple(D.shape), dtype=tdt, device=dev)
+        for _ in range(2):
+            dist.all_gather_into_tensor(gathered, D)
+        torch.cuda.synchronize()
+        dist.barrier()
+        g0 = torch.cuda.Event(enable_timing=True)
+        g1 = torch.cuda.Event(enable_timing=True)
+        g0.record(stream)
+        reps = 5
+        for _ in range(reps):
+            dist.all_gather_into_tensor(gathered, D)
+        g1.record(stream)
+        torch.cuda.synchronize()
+        ag_ms = g0.elapsed_time(g1) / reps
+        t = torch.tensor([ag_ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ag_ms = float(t.item())
+        nbytes = D.numel() * D.element_size()
+        allgather = {"ms": ag_ms, "bytes_per_rank": nbytes,
+                     "bus_gbs": nbytes * (world - 1) / (ag_ms * 1e-3) / 1e9}
+        del gathered
+
+    # ---- CPU baseline (rank 0, N=1 only) ----
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        v, kind_s, cores, sample, _ = cpu_reference_sample(args.config, target_s=args.ref_seconds)
+        cpu = {"value": v, "unit": "TFLOPS", "cores": cores, "kind": kind_s, "sample": sample}
+
+    bf16_peak, hbm_peak, basis = load_peaks()
+    peak = 2.0 * bf16_peak
+    kernel_ms = min(per)  # dominant kernel: the GEMM (plus the split-K reduce when routed)
+    achieved = flops_rank / (ms * 1e-3) / 1e12
+    route = lib.choose_tile(M, N, Kp)
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "TFLOPS", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "fp6_e2m3 x fp6_e2m3 -> f32 accumulate",
+            "data": "synthetic (seeded E2M3 codes uniform over 64 codes, E8M0 exponents per BASELINE)",
+            "config": {"workload": CONFIG_DESC[args.config] + (f", N-sharded over {world} GPUs (per-GPU shard N={N})"
+                                                               if world > 1 else ""),
+                       "M": M, "N_per_gpu": N, "N_total": N * world, "K": K, "out": out_name,
+                       "route": {"MT": route.MT, "NT": route.NT, "splits": max(1, wsb // (M * N * 4))},
+                       "parallelism": f"N-sharded x{world}, no collective on the GEMM path",
+                       "l2": "256 MiB buffer written before every timed step (L2 flushed)"},
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                         "frac": achieved / peak, "traffic": None,
+                         "peak_basis": f"2 x {basis} cuBLAS bf16 dense ({bf16_peak:.1f} TFLOP/s): B200's dense "
+                                       f"FP8/FP6 tensor rate is twice bf16",
+                         "best_step_ms": kernel_ms},
+            "cpu_baseline": cpu,
+            "e2e": {"value": e2e_value, "unit": "TFLOPS", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "ms_per_step": e2e_ms, "path": "pinned host -> H2D copies -> mxfp6_gemm (C ABI) -> D2H"},
+            "gpu_launches": launches,
+            "clocks": clk.summary(),
+            "device_status": status,
+        }
+        if allgather:
+            line["allgather"] = allgather
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--config", choices=sorted(CONFIGS), default="cfg2")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--no-allgather", action="store_true")
+    ap.add_argument("--ref-seconds", type=float, default=10.0, help="target CPU seconds per reference sample")
+    args = ap.parse_args()
+    if args.warmup < 3 and args.impl == "ours":
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference_arm(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

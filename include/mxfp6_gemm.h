@@ -1,0 +1,126 @@
+/* C ABI of libmxfp6gemm (B200, sm_100a).
+ *
+ * Plain pointers and sizes only; no CUDA or torch types. Every entry point mirrors one of the
+ * reference library's C++ entry points (eeezio/mxfp6-gemm, paths relative to that project) so a
+ * foreign-function binding (ctypes, cgo, JNI, ...) can drive the same path:
+ *
+ *   mxfp6_gemm                  <- mxfp6::gemm                 include/mxfp6/gemm.hpp:63-64
+ *   mxfp6_gemm_workspace_size   <- mxfp6::gemm_workspace_size  include/mxfp6/gemm.hpp:53
+ *   mxfp6_choose_tile           <- mxfp6::choose_tile          include/mxfp6/gemm.hpp:46
+ *   mxfp6_kpad / mxfp6_k_tile   <- mxfp6::kpad / K_TILE        include/mxfp6/gemm.hpp:30-33
+ *   mxfp6_gemm_force_tile       <- mxfp6::gemm_force_tile      src/gemm.cpp:89-107 (test hook)
+ *
+ * Additions with no counterpart in the reference (it returns void and never checks errors):
+ *   mxfp6_gemm_stream     the same call on an explicit cudaStream_t (passed as void*).
+ *   mxfp6_last_error      status of the last call on this thread (0 = ok).
+ *   mxfp6_device_status   synchronises the device and returns/clears the kernel status word
+ *                         (bounded waits inside the kernel record timeouts there).
+ *
+ * Host preprocessing helpers (the C face of mxfp6/preprocess.hpp, used by bindings that cannot
+ * instantiate the C++ header) are declared at the end.
+ */
+#ifndef MXFP6_GEMM_H_
+#define MXFP6_GEMM_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Output element type; values match mxfp6::OutType. */
+enum mxfp6_out_type { MXFP6_OUT_F32 = 0, MXFP6_OUT_F16 = 1, MXFP6_OUT_BF16 = 2 };
+
+/* Error codes returned by mxfp6_last_error(). */
+enum mxfp6_status {
+    MXFP6_OK = 0,
+    MXFP6_ERR_INVALID_SHAPE = 1,     /* M, N or Kp not a positive multiple of 128 */
+    MXFP6_ERR_INVALID_STRIDE = 2,    /* row bytes < 0.75*Kp or not a multiple of 32 */
+    MXFP6_ERR_MISALIGNED = 3,        /* a pointer violates its alignment rule */
+    MXFP6_ERR_NULL_POINTER = 4,      /* a required pointer is null */
+    MXFP6_ERR_INVALID_OUT_TYPE = 5,  /* ot not one of mxfp6_out_type */
+    MXFP6_ERR_CUDA = 6,              /* a CUDA runtime / driver call failed */
+    MXFP6_ERR_DEVICE_TIMEOUT = 7,    /* a kernel wait hit its bound (see mxfp6_device_status) */
+    MXFP6_ERR_WORKSPACE = 8,         /* workspace too small for a forced split */
+    MXFP6_ERR_UNSUPPORTED = 9        /* route / option not available on this device */
+};
+
+/* Device status bits written by kernels (mxfp6_device_status). */
+#define MXFP6_DEV_TIMEOUT_PRODUCER 0x1u /* TMA producer: an empty slot never came back */
+#define MXFP6_DEV_TIMEOUT_MMA 0x2u      /* MMA issuer: a full slot or free accumulator never came */
+#define MXFP6_DEV_TIMEOUT_EPILOGUE 0x4u /* epilogue: an accumulator was never committed */
+#define MXFP6_DEV_TIMEOUT_DRAIN 0x8u    /* abort path: in-flight copies or MMAs did not settle */
+
+/* D[M,N] = A[M,K]·B[K,N] on the legacy default stream. ot: mxfp6_out_type. See
+ * include/mxfp6/gemm.hpp for layouts and requirements. On a validation error nothing is
+ * launched, a message goes to stderr and mxfp6_last_error() returns the code. */
+void mxfp6_gemm(int ot, int M, int N, int Kp, const void* dA, const void* dBsh, const uint8_t* dsA,
+                const uint8_t* dsB, void* dD, int A_row_bytes, int B_row_bytes, void* ws,
+                size_t ws_bytes);
+
+/* Same as mxfp6_gemm on an explicit stream (a cudaStream_t passed as void*; NULL = legacy). */
+void mxfp6_gemm_stream(int ot, int M, int N, int Kp, const void* dA, const void* dBsh,
+                       const uint8_t* dsA, const uint8_t* dsB, void* dD, int A_row_bytes,
+                       int B_row_bytes, void* ws, size_t ws_bytes, void* stream);
+
+/* Split-K workspace bytes gemm() wants for (M,N,Kp); 0 when the route does not split. */
+size_t mxfp6_gemm_workspace_size(int M, int N, int Kp);
+
+/* Route for (M,N,Kp): writes MT, NT, MPW, NPW into out[0..3]. */
+void mxfp6_choose_tile(int M, int N, int Kp, int* out4);
+
+/* K granule (128) and K padded to it. */
+int mxfp6_k_tile(void);
+int mxfp6_kpad(int K);
+
+/* Test hook (reference: src/gemm.cpp:89-107 gemm_force_tile): run a specific tile width and
+ * split factor instead of the routed one. NT in {128, 256}; splits >= 1 (splits > 1 needs
+ * ws_bytes >= splits*M*N*4). Same validation as mxfp6_gemm; stream may be NULL. */
+void mxfp6_gemm_force_tile(int ot, int M, int N, int Kp, int NT, int splits, const void* dA,
+                           const void* dBsh, const uint8_t* dsA, const uint8_t* dsB, void* dD,
+                           int A_row_bytes, int B_row_bytes, void* ws, size_t ws_bytes,
+                           void* stream);
+
+/* Status of the last mxfp6_* call on this thread, and a static message for it. */
+int mxfp6_last_error(void);
+const char* mxfp6_last_error_string(void);
+
+/* Synchronises the current device, returns the sticky kernel status bits (MXFP6_DEV_*) and
+ * clears them. Returns -1 if the synchronisation itself failed. */
+int mxfp6_device_status(void);
+
+/* Number of kernels this library has launched in this process (all devices). */
+uint64_t mxfp6_launch_count(void);
+
+/* ---- host preprocessing (C face of include/mxfp6/preprocess.hpp) --------------------------
+ * All buffers are host memory, caller-allocated. Sizes: packed row = 3*cols/4 bytes,
+ * raw scales = rows*(cols/32) bytes, tiled scales = mxfp6_tiled_scale_bytes(rows, cols). */
+
+/* quantize_to_mxfp6 (reference: include/mxfp6/preprocess.hpp:51-97): float [rows][cols]
+ * (cols % 32 == 0) -> packed FP6 [rows][3*cols/4] + raw E8M0 scales [rows][cols/32].
+ * nthreads <= 0 uses all hardware threads; the result does not depend on it. */
+void mxfp6_quantize(const float* mat, int rows, int cols, uint8_t* packed, uint8_t* scales,
+                    int nthreads);
+
+/* dequantize_mxfp6 (reference: include/mxfp6/preprocess.hpp:100-109). */
+void mxfp6_dequantize(const uint8_t* packed, const uint8_t* scales, int rows, int cols,
+                      float* out);
+
+/* Bytes of the tiled scale layout for a [rows][cols/32] raw scale matrix (cols % 128 == 0):
+ * ceil(rows/128) * (cols/128) * 512. */
+size_t mxfp6_tiled_scale_bytes(int rows, int cols);
+
+/* preprocess_scale + tile_scale (reference: include/mxfp6/preprocess.hpp:136-162,216-233):
+ * raw scales [rows][cols/32] -> B200 atom layout. Rows past `rows` in the last atom get the
+ * finite code 127. */
+void mxfp6_tile_scales(const uint8_t* scales, int rows, int cols, uint8_t* tiled);
+
+/* Inverse of mxfp6_tile_scales (for checks). */
+void mxfp6_untile_scales(const uint8_t* tiled, int rows, int cols, uint8_t* scales);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MXFP6_GEMM_H_ */

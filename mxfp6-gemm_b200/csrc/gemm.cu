@@ -1,0 +1,374 @@
+// libmxfp6gemm host side: validation, routing, tensor-map construction and launches.
+//
+// Counterparts in the reference (paths within eeezio/mxfp6-gemm):
+//   mxfp6::gemm / gemm_workspace_size / choose_tile   src/gemm.cpp:12-83
+//   detail::splitk_S / dispatch_gemm                  src/dispatch.hpp:30-187
+//   gemm_force_tile (test hook)                       src/gemm.cpp:89-107
+// The reference routes over four gfx950 tiles with a 256-CU wave table; this file routes over
+// the B200 kernel's two tile widths with a wave-count cost model on the device's SM count.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <atomic>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include "gemm_kernel.cuh"
+#include "mxfp6/gemm.hpp"
+#include "mxfp6_gemm.h"
+#include "route.hpp"
+
+namespace mxfp6 {
+
+namespace {
+
+thread_local int t_last_error = MXFP6_OK;
+std::atomic<uint64_t> g_launches{0};
+
+void set_error(int code, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
+void set_error(int code, const char* fmt, ...) {
+    t_last_error = code;
+    va_list ap;
+    va_start(ap, fmt);
+    std::fprintf(stderr, "[mxfp6] ");
+    std::vfprintf(stderr, fmt, ap);
+    std::fprintf(stderr, "\n");
+    va_end(ap);
+}
+
+// ---- device properties ------------------------------------------------------------------------
+
+constexpr int kMaxDevices = 64;
+int g_sm_count[kMaxDevices];
+std::once_flag g_sm_once[kMaxDevices];
+
+int current_device() {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return -1;
+    return dev;
+}
+
+// SM count of the current device; 148 (B200) when no device is visible, so host-only queries
+// (choose_tile, gemm_workspace_size) stay answerable on a machine without a GPU.
+int sm_count() {
+    int dev = current_device();
+    if (dev < 0 || dev >= kMaxDevices) {
+        cudaGetLastError();
+        return 148;
+    }
+    std::call_once(g_sm_once[dev], [dev] {
+        int n = 0;
+        if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
+            n = 148;
+        g_sm_count[dev] = n;
+    });
+    return g_sm_count[dev];
+}
+
+// ---- tensor maps ---------------------------------------------------------------------------------
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            p = nullptr;
+        return reinterpret_cast<EncodeTiledFn>(p);
+    }();
+    return fn;
+}
+
+// Packed FP6 matrix [rows][Kp] with row_bytes stride, read in 128 (K) x box_rows boxes through
+// the 16U6 unpack mode with 128-byte swizzle.
+bool make_fp6_tmap(CUtensorMap* map, const void* ptr, int rows, int Kp, int row_bytes, int box_rows) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return false;
+    cuuint64_t dims[2] = {(cuuint64_t)Kp, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)row_bytes};
+    cuuint32_t box[2] = {128u, (cuuint32_t)box_rows};
+    cuuint32_t estr[2] = {1u, 1u};
+    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_16U6_ALIGN16B, 2, const_cast<void*>(ptr), dims,
+                    strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
+// ---- validation -----------------------------------------------------------------------------------
+
+bool aligned(const void* p, uintptr_t a) {
+    return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0;
+}
+
+bool validate(int ot, int M, int N, int Kp, const void* dA, const void* dB, const void* sA,
+              const void* sB, const void* dD, int A_row_bytes, int B_row_bytes) {
+    if (ot < MXFP6_OUT_F32 || ot > MXFP6_OUT_BF16) {
+        set_error(MXFP6_ERR_INVALID_OUT_TYPE, "invalid output type %d", ot);
+        return false;
+    }
+    if (M <= 0 || N <= 0 || Kp <= 0 || M % 128 || N % 128 || Kp % K_TILE) {
+        set_error(MXFP6_ERR_INVALID_SHAPE,
+                  "unsupported shape %dx%dx%d: M and N must be positive multiples of 128 and Kp a "
+                  "positive multiple of %d (pad with kpad())",
+                  M, N, Kp, K_TILE);
+        return false;
+    }
+    const long long need = (long long)Kp * 3 / 4;
+    if (A_row_bytes < need || B_row_bytes < need || A_row_bytes % 32 || B_row_bytes % 32) {
+        set_error(MXFP6_ERR_INVALID_STRIDE,
+                  "row strides A=%d B=%d bytes: each must be >= %lld (= 0.75*Kp) and a multiple of "
+                  "32 for the tensor-memory accelerator's FP6 unpack mode",
+                  A_row_bytes, B_row_bytes, need);
+        return false;
+    }
+    if (!dA || !dB || !sA || !sB || !dD) {
+        set_error(MXFP6_ERR_NULL_POINTER, "null device pointer (A=%p B=%p sA=%p sB=%p D=%p)", dA, dB,
+                  sA, sB, dD);
+        return false;
+    }
+    if (!aligned(dA, 32) || !aligned(dB, 32) || !aligned(sA, 16) || !aligned(sB, 16) || !aligned(dD, 16)) {
+        set_error(MXFP6_ERR_MISALIGNED,
+                  "misaligned pointer: A and B need 32-byte, scales and D 16-byte alignment");
+        return false;
+    }
+    return true;
+}
+
+// ---- launch ----------------------------------------------------------------------------------------
+
+template <int BN, typename OutT, bool PARTIAL>
+bool launch_gemm(int M, int N, int Kp, const void* dA, const void* dB, const uint8_t* sA,
+                 const uint8_t* sB, void* dD, float* ws, int A_row_bytes, int B_row_bytes, int splits,
+                 cudaStream_t stream) {
+    using C = kern::Config<BN>;
+    auto kernel = kern::gemm_mxfp6_sm100<BN, OutT, PARTIAL>;
+    static std::once_flag attr_once[kMaxDevices];
+    const int dev = current_device();
+    if (dev < 0 || dev >= kMaxDevices) {
+        set_error(MXFP6_ERR_CUDA, "no CUDA device");
+        return false;
+    }
+    cudaError_t attr_err = cudaSuccess;
+    std::call_once(attr_once[dev], [&] {
+        attr_err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
+    });
+    if (attr_err != cudaSuccess) {
+        set_error(MXFP6_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(attr_err));
+        return false;
+    }
+    CUtensorMap tmA, tmB;
+    if (!make_fp6_tmap(&tmA, dA, M, Kp, A_row_bytes, kern::BM) ||
+        !make_fp6_tmap(&tmB, dB, N, Kp, B_row_bytes, BN)) {
+        set_error(MXFP6_ERR_CUDA, "cuTensorMapEncodeTiled failed for %dx%dx%d", M, N, Kp);
+        return false;
+    }
+    kern::Params p;
+    p.sfA = sA;
+    p.sfB = sB;
+    p.D = dD;
+    p.ws = ws;
+    p.M = M;
+    p.N = N;
+    p.Kp = Kp;
+    p.m_blocks = M / kern::BM;
+    p.n_blocks = (N + BN - 1) / BN;
+    p.k_slabs = Kp / kern::BK;
+    p.splits = splits;
+    const long long tiles = (long long)p.m_blocks * p.n_blocks * splits;
+    const int grid = (int)(tiles < sm_count() ? tiles : sm_count());
+    kernel<<<grid, kern::NUM_THREADS, C::SMEM_BYTES, stream>>>(tmA, tmB, p);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) {
+        set_error(MXFP6_ERR_CUDA, "GEMM launch failed: %s", cudaGetErrorString(e));
+        return false;
+    }
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+    return true;
+}
+
+template <typename OutT>
+bool launch_reduce(const float* ws, void* dD, int M, int N, int splits, cudaStream_t stream) {
+    const long long total = (long long)M * N;
+    const long long n4 = total / 4;
+    long long blocks = (n4 + 255) / 256;
+    const long long cap = (long long)sm_count() * 8;
+    if (blocks > cap) blocks = cap;
+    kern::reduce_partials<OutT><<<(int)blocks, 256, 0, stream>>>(ws, static_cast<OutT*>(dD), total, splits);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) {
+        set_error(MXFP6_ERR_CUDA, "split-K reduce launch failed: %s", cudaGetErrorString(e));
+        return false;
+    }
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+    return true;
+}
+
+template <typename OutT>
+bool run_typed(int M, int N, int Kp, int NT, int splits, const void* dA, const void* dB,
+               const uint8_t* sA, const uint8_t* sB, void* dD, int Ar, int Br, void* ws,
+               cudaStream_t stream) {
+    float* wsf = static_cast<float*>(ws);
+    if (splits > 1) {
+        bool ok = NT == 256 ? launch_gemm<256, OutT, true>(M, N, Kp, dA, dB, sA, sB, dD, wsf, Ar, Br, splits, stream)
+                            : launch_gemm<128, OutT, true>(M, N, Kp, dA, dB, sA, sB, dD, wsf, Ar, Br, splits, stream);
+        return ok && launch_reduce<OutT>(wsf, dD, M, N, splits, stream);
+    }
+    return NT == 256 ? launch_gemm<256, OutT, false>(M, N, Kp, dA, dB, sA, sB, dD, wsf, Ar, Br, 1, stream)
+                     : launch_gemm<128, OutT, false>(M, N, Kp, dA, dB, sA, sB, dD, wsf, Ar, Br, 1, stream);
+}
+
+bool run(int ot, int M, int N, int Kp, int NT, int splits, const void* dA, const void* dB,
+         const uint8_t* sA, const uint8_t* sB, void* dD, int Ar, int Br, void* ws, cudaStream_t stream) {
+    switch (ot) {
+        case MXFP6_OUT_F32:
+            return run_typed<float>(M, N, Kp, NT, splits, dA, dB, sA, sB, dD, Ar, Br, ws, stream);
+        case MXFP6_OUT_F16:
+            return run_typed<__half>(M, N, Kp, NT, splits, dA, dB, sA, sB, dD, Ar, Br, ws, stream);
+        default:
+            return run_typed<__nv_bfloat16>(M, N, Kp, NT, splits, dA, dB, sA, sB, dD, Ar, Br, ws, stream);
+    }
+}
+
+void gemm_entry(int ot, int M, int N, int Kp, const void* dA, const void* dB, const uint8_t* sA,
+                const uint8_t* sB, void* dD, int Ar, int Br, void* ws, size_t ws_bytes,
+                cudaStream_t stream) {
+    t_last_error = MXFP6_OK;
+    if (!validate(ot, M, N, Kp, dA, dB, sA, sB, dD, Ar, Br)) return;
+    Route r = route_for(M, N, Kp, sm_count());
+    if (r.splits > 1) {
+        const size_t need = splitk_bytes(M, N, r.splits);
+        if (!ws || ws_bytes < need || !aligned(ws, 16)) {
+            // Same contract as the reference (src/dispatch.hpp:76-87): correct, only slower.
+            std::fprintf(stderr,
+                         "[mxfp6] split-K skipped for %dx%dx%d: workspace %zu bytes, need %zu — "
+                         "running unsplit (slower). Size it with gemm_workspace_size().\n",
+                         M, N, Kp, ws_bytes, need);
+            r.splits = 1;
+        }
+    }
+    run(ot, M, N, Kp, r.NT, r.splits, dA, dB, sA, sB, dD, Ar, Br, ws, stream);
+}
+
+}  // namespace
+
+// ---- C++ API ------------------------------------------------------------------------------------------
+
+TileChoice choose_tile(int M, int N, int Kp) {
+    Route r = route_for(M, N, Kp, sm_count());
+    return TileChoice{128, r.NT, 128 / 32, r.NT / 32};
+}
+
+size_t gemm_workspace_size(int M, int N, int Kp) {
+    Route r = route_for(M, N, Kp, sm_count());
+    return r.splits > 1 ? splitk_bytes(M, N, r.splits) : 0;
+}
+
+void gemm(OutType ot, int M, int N, int Kp, const void* dA, const void* dBsh, const uint8_t* dsA,
+          const uint8_t* dsB, void* dD, int A_row_bytes, int B_row_bytes, void* ws, size_t ws_bytes) {
+    gemm_entry((int)ot, M, N, Kp, dA, dBsh, dsA, dsB, dD, A_row_bytes, B_row_bytes, ws, ws_bytes, 0);
+}
+
+}  // namespace mxfp6
+
+// ---- C ABI --------------------------------------------------------------------------------------------
+
+using namespace mxfp6;
+
+extern "C" {
+
+void mxfp6_gemm(int ot, int M, int N, int Kp, const void* dA, const void* dBsh, const uint8_t* dsA,
+                const uint8_t* dsB, void* dD, int A_row_bytes, int B_row_bytes, void* ws,
+                size_t ws_bytes) {
+    gemm_entry(ot, M, N, Kp, dA, dBsh, dsA, dsB, dD, A_row_bytes, B_row_bytes, ws, ws_bytes, 0);
+}
+
+void mxfp6_gemm_stream(int ot, int M, int N, int Kp, const void* dA, const void* dBsh,
+                       const uint8_t* dsA, const uint8_t* dsB, void* dD, int A_row_bytes,
+                       int B_row_bytes, void* ws, size_t ws_bytes, void* stream) {
+    gemm_entry(ot, M, N, Kp, dA, dBsh, dsA, dsB, dD, A_row_bytes, B_row_bytes, ws, ws_bytes,
+               static_cast<cudaStream_t>(stream));
+}
+
+size_t mxfp6_gemm_workspace_size(int M, int N, int Kp) {
+    return gemm_workspace_size(M, N, Kp);
+}
+
+void mxfp6_choose_tile(int M, int N, int Kp, int* out4) {
+    TileChoice t = choose_tile(M, N, Kp);
+    if (out4) {
+        out4[0] = t.MT;
+        out4[1] = t.NT;
+        out4[2] = t.MPW;
+        out4[3] = t.NPW;
+    }
+}
+
+int mxfp6_k_tile(void) {
+    return K_TILE;
+}
+
+int mxfp6_kpad(int K) {
+    return kpad(K);
+}
+
+void mxfp6_gemm_force_tile(int ot, int M, int N, int Kp, int NT, int splits, const void* dA,
+                           const void* dBsh, const uint8_t* dsA, const uint8_t* dsB, void* dD,
+                           int A_row_bytes, int B_row_bytes, void* ws, size_t ws_bytes,
+                           void* stream) {
+    t_last_error = MXFP6_OK;
+    if (!validate(ot, M, N, Kp, dA, dBsh, dsA, dsB, dD, A_row_bytes, B_row_bytes)) return;
+    if ((NT != 128 && NT != 256) || splits < 1 || splits > Kp / K_TILE) {
+        set_error(MXFP6_ERR_UNSUPPORTED, "forced route NT=%d splits=%d not available for Kp=%d", NT,
+                  splits, Kp);
+        return;
+    }
+    if (splits > 1 && (!ws || ws_bytes < splitk_bytes(M, N, splits) || !aligned(ws, 16))) {
+        set_error(MXFP6_ERR_WORKSPACE, "forced split %d needs %zu workspace bytes, got %zu", splits,
+                  splitk_bytes(M, N, splits), ws_bytes);
+        return;
+    }
+    run(ot, M, N, Kp, NT, splits, dA, dBsh, dsA, dsB, dD, A_row_bytes, B_row_bytes, ws,
+        static_cast<cudaStream_t>(stream));
+}
+
+int mxfp6_last_error(void) {
+    return t_last_error;
+}
+
+const char* mxfp6_last_error_string(void) {
+    switch (t_last_error) {
+        case MXFP6_OK: return "ok";
+        case MXFP6_ERR_INVALID_SHAPE: return "invalid shape";
+        case MXFP6_ERR_INVALID_STRIDE: return "invalid row stride";
+        case MXFP6_ERR_MISALIGNED: return "misaligned pointer";
+        case MXFP6_ERR_NULL_POINTER: return "null pointer";
+        case MXFP6_ERR_INVALID_OUT_TYPE: return "invalid output type";
+        case MXFP6_ERR_CUDA: return "CUDA error";
+        case MXFP6_ERR_DEVICE_TIMEOUT: return "device wait timed out";
+        case MXFP6_ERR_WORKSPACE: return "workspace too small";
+        case MXFP6_ERR_UNSUPPORTED: return "unsupported route";
+        default: return "unknown error";
+    }
+}
+
+int mxfp6_device_status(void) {
+    if (cudaDeviceSynchronize() != cudaSuccess) return -1;
+    unsigned int v = 0, zero = 0;
+    if (cudaMemcpyFromSymbol(&v, g_device_status, sizeof(v)) != cudaSuccess) return -1;
+    if (cudaMemcpyToSymbol(g_device_status, &zero, sizeof(zero)) != cudaSuccess) return -1;
+    if (v) t_last_error = MXFP6_ERR_DEVICE_TIMEOUT;
+    return (int)v;
+}
+
+uint64_t mxfp6_launch_count(void) {
+    return g_launches.load(std::memory_order_relaxed);
+}
+
+}  // extern "C"

@@ -1,0 +1,387 @@
+#pragma once
+// The B200 MXFP6 GEMM kernel: persistent, warp-specialised, block-scaled tcgen05 MMA.
+//
+// Replaces the reference's lds_gemm_hybrid_dripA (reference: src/kernel.hpp:73-300) and, in
+// partial mode, its split-K first stage; reduce_splitk (reference: src/kernel.hpp:305-313) is
+// reduce_partials() below. The math is the same: for every output element
+//   D[m][n] = sum over K-blocks b of 2^(sa[m][b]-127) * 2^(sb[n][b]-127) * sum_k a[m][k] * b[n][k]
+// accumulated in FP32 and converted once to the output type; the schedule is B200's:
+//
+//   warp 0 (one lane)  TMA producer: per 128-wide K slab, one 2-D tensor load of A (128 rows)
+//                      and of B^T (BN rows) in the 16U6 unpack mode (packed FP6 in HBM -> one
+//                      byte per code in shared memory, 128-byte swizzle), plus untiled bulk
+//                      loads of the 512-byte scale atoms, into a STAGES-deep mbarrier ring.
+//   warp 1 (one lane)  MMA issuer: tcgen05.cp of the scale atoms into tensor memory, then four
+//                      tcgen05.mma.kind::mxf8f6f4.block_scale (K = 32 each) per slab into an
+//                      FP32 accumulator of 128 lanes x BN columns in tensor memory; tcgen05.commit
+//                      returns the ring slot and, after the last slab, hands the tile to:
+//   warps 2..5         epilogue: tcgen05.ld 32 columns at a time (warp w owns lanes 32*(w%4)..),
+//                      convert to FP32 / FP16 / BF16 (round to nearest even) and store; in
+//                      partial mode store FP32 partial sums into the split-K workspace.
+//
+// Tiles (128 x BN output blocks, times the split-K factor) are handed out round-robin over a
+// persistent grid of at most one CTA per SM, in groups of GROUP_M row-blocks for L2 reuse.
+// Every wait is bounded; a timeout sets a bit in the device status word, makes the other roles
+// leave their loops, lets in-flight copies and MMAs settle (again bounded) and frees tensor
+// memory before the CTA exits.
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <type_traits>
+
+#include "sm100_ptx.cuh"
+
+namespace mxfp6 {
+
+// Sticky status bits written by kernels (MXFP6_DEV_* in mxfp6_gemm.h). This header is compiled
+// into exactly one translation unit (gemm.cu), which owns the definition.
+__device__ unsigned int g_device_status = 0;
+
+namespace kern {
+
+constexpr int BM = 128;             // output rows per tile (tensor-memory lanes)
+constexpr int BK = 128;             // K elements per pipeline slab
+constexpr int GROUP_M = 8;          // row-blocks per rasterisation group
+constexpr int NUM_THREADS = 192;    // 6 warps
+constexpr int EPI_WARP0 = 2;        // first epilogue warp
+constexpr int A_TMA_BYTES = BM * BK * 3 / 4;  // packed bytes one A slab moves
+constexpr long long WAIT_BUDGET = 4000000000LL;  // cycles (about 2 s at 1.9 GHz)
+
+template <int BN>
+struct Config {
+    static_assert(BN == 128 || BN == 256, "tile width");
+    static constexpr int STAGES = BN == 256 ? 4 : 6;
+    static constexpr int A_BYTES = BM * BK;  // one byte per code in shared memory
+    static constexpr int B_BYTES = BN * BK;
+    static constexpr int AB_STAGE = A_BYTES + B_BYTES;
+    static constexpr int SFA_BYTES = 512;
+    static constexpr int SFB_ATOMS = BN / 128;
+    static constexpr int SF_STAGE = SFA_BYTES + SFB_ATOMS * 512;
+    static constexpr int B_TMA_BYTES = BN * BK * 3 / 4;
+    // tensor-memory columns: accumulator [0,BN), A scales [BN, BN+4), B scales after them
+    static constexpr int TMEM_SFA = BN;
+    static constexpr int TMEM_SFB = BN + 4;
+    static constexpr int TMEM_COLS = BN == 256 ? 512 : 256;
+    static constexpr int BAR_BYTES = 256;
+    static constexpr int SMEM_BYTES = 1024 + STAGES * (AB_STAGE + SF_STAGE) + BAR_BYTES;
+    static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
+};
+
+struct Params {
+    const uint8_t* sfA;  // A scales, atom layout
+    const uint8_t* sfB;  // B scales, atom layout
+    void* D;             // output (OutT) or nullptr in partial mode
+    float* ws;           // FP32 partials [splits][M][N] in partial mode
+    int M, N, Kp;
+    int m_blocks, n_blocks, k_slabs, splits;
+};
+
+struct TileCoord {
+    int mb, nb, split, kb_begin, kb_count;
+};
+
+__device__ __forceinline__ TileCoord decode_tile(int t, const Params& p) {
+    const int tiles_mn = p.m_blocks * p.n_blocks;
+    TileCoord c;
+    c.split = t / tiles_mn;
+    const int mn = t - c.split * tiles_mn;
+    const int group_tiles = GROUP_M * p.n_blocks;
+    const int g = mn / group_tiles;
+    const int first_m = g * GROUP_M;
+    const int gm = min(p.m_blocks - first_m, GROUP_M);
+    const int within = mn - g * group_tiles;
+    c.mb = first_m + within % gm;
+    c.nb = within / gm;
+    const int per = p.k_slabs / p.splits, rem = p.k_slabs % p.splits;
+    c.kb_begin = c.split * per + min(c.split, rem);
+    c.kb_count = per + (c.split < rem ? 1 : 0);
+    return c;
+}
+
+__device__ __forceinline__ void raise_status(unsigned int bit, volatile int* abort_flag) {
+    atomicOr(&g_device_status, bit);
+    *abort_flag = 1;
+}
+
+template <typename OutT>
+__device__ __forceinline__ void store_row_chunk(OutT* dst, const uint32_t (&r)[32]);
+
+template <>
+__device__ __forceinline__ void store_row_chunk<float>(float* dst, const uint32_t (&r)[32]) {
+    uint4* d = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+    for (int i = 0; i < 8; i++) d[i] = make_uint4(r[4 * i], r[4 * i + 1], r[4 * i + 2], r[4 * i + 3]);
+}
+
+template <>
+__device__ __forceinline__ void store_row_chunk<__half>(__half* dst, const uint32_t (&r)[32]) {
+    uint32_t h[16];
+#pragma unroll
+    for (int i = 0; i < 16; i++) {
+        __half2 v = __floats2half2_rn(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1]));
+        h[i] = *reinterpret_cast<uint32_t*>(&v);
+    }
+    uint4* d = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+    for (int i = 0; i < 4; i++) d[i] = make_uint4(h[4 * i], h[4 * i + 1], h[4 * i + 2], h[4 * i + 3]);
+}
+
+template <>
+__device__ __forceinline__ void store_row_chunk<__nv_bfloat16>(__nv_bfloat16* dst,
+                                                               const uint32_t (&r)[32]) {
+    uint32_t h[16];
+#pragma unroll
+    for (int i = 0; i < 16; i++) {
+        __nv_bfloat162 v =
+            __floats2bfloat162_rn(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1]));
+        h[i] = *reinterpret_cast<uint32_t*>(&v);
+    }
+    uint4* d = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+    for (int i = 0; i < 4; i++) d[i] = make_uint4(h[4 * i], h[4 * i + 1], h[4 * i + 2], h[4 * i + 3]);
+}
+
+// OutT: float / __half / __nv_bfloat16. PARTIAL: write FP32 partial sums to p.ws instead of D.
+template <int BN, typename OutT, bool PARTIAL>
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    gemm_mxfp6_sm100(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                     const Params p) {
+    using C = Config<BN>;
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    // 1024-byte alignment for the 128-byte-swizzled operand tiles.
+    const uint32_t raw_u32 = sm100::smem_u32(smem_raw);
+    const uint32_t base = (raw_u32 + 1023u) & ~1023u;
+    uint8_t* base_ptr = smem_raw + (base - raw_u32);
+
+    const uint32_t ab_base = base;                                   // STAGES x (A | B)
+    const uint32_t sf_base = base + C::STAGES * C::AB_STAGE;         // STAGES x (sfA | sfB)
+    const uint32_t bar_base = sf_base + C::STAGES * C::SF_STAGE;     // barriers
+    uint8_t* bar_ptr = base_ptr + (bar_base - base);
+    // barrier map (8 bytes each): full[S], empty[S], acc_full, acc_empty, drain
+    auto full_bar = [&](int s) { return bar_base + 8u * s; };
+    auto empty_bar = [&](int s) { return bar_base + 8u * (C::STAGES + s); };
+    const uint32_t acc_full = bar_base + 8u * (2 * C::STAGES);
+    const uint32_t acc_empty = acc_full + 8u;
+    const uint32_t drain_bar = acc_full + 16u;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_ptr + 8 * (2 * C::STAGES + 3));
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(bar_ptr + 8 * (2 * C::STAGES + 3) + 8);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < C::STAGES; s++) {
+            sm100::mbar_init(full_bar(s), 1);
+            sm100::mbar_init(empty_bar(s), 1);
+        }
+        sm100::mbar_init(acc_full, 1);
+        sm100::mbar_init(acc_empty, 4 * 32);
+        sm100::mbar_init(drain_bar, 1);
+        *abort_flag = 0;
+        sm100::fence_mbar_init();
+        sm100::fence_async_shared();
+        sm100::prefetch_tmap(&tmA);
+        sm100::prefetch_tmap(&tmB);
+    }
+    if (warp == 1) {
+        sm100::tmem_alloc(sm100::smem_u32(tmem_slot), C::TMEM_COLS);
+        sm100::tmem_relinquish();
+    }
+    sm100::tc_fence_before();
+    __syncthreads();
+    sm100::tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    const int total_tiles = p.m_blocks * p.n_blocks * p.splits;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            // ---------------- TMA producer ----------------
+            int stage = 0;
+            uint32_t phase = 0;
+            uint32_t issued_mask = 0, issued_phase = 0;  // per stage: outstanding load + parity
+            bool ok = true;
+            for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
+                const TileCoord tc = decode_tile(t, p);
+                int sfb_atoms = 0;
+#pragma unroll
+                for (int j = 0; j < C::SFB_ATOMS; j++)
+                    if (tc.nb * BN + j * 128 < p.N) sfb_atoms++;
+                const uint32_t tx = A_TMA_BYTES + C::B_TMA_BYTES + 512u * (1 + sfb_atoms);
+                for (int i = 0; i < tc.kb_count; i++) {
+                    if (!sm100::wait_parity_bounded(empty_bar(stage), phase ^ 1u, abort_flag,
+                                                    WAIT_BUDGET)) {
+                        if (!*abort_flag) raise_status(0x1u, abort_flag);
+                        ok = false;
+                        break;
+                    }
+                    const int kb = tc.kb_begin + i;
+                    const uint32_t fb = full_bar(stage);
+                    sm100::mbar_arrive_expect_tx(fb, tx);
+                    const uint32_t a_dst = ab_base + stage * C::AB_STAGE;
+                    sm100::tma_load_2d(a_dst, &tmA, fb, kb * BK, tc.mb * BM);
+                    sm100::tma_load_2d(a_dst + C::A_BYTES, &tmB, fb, kb * BK, tc.nb * BN);
+                    const uint32_t sf_dst = sf_base + stage * C::SF_STAGE;
+                    sm100::bulk_load(sf_dst, p.sfA + ((size_t)tc.mb * p.k_slabs + kb) * 512, 512, fb);
+                    for (int j = 0; j < sfb_atoms; j++)
+                        sm100::bulk_load(
+                            sf_dst + 512 + 512 * j,
+                            p.sfB + ((size_t)(tc.nb * C::SFB_ATOMS + j) * p.k_slabs + kb) * 512, 512, fb);
+                    issued_mask |= 1u << stage;
+                    issued_phase = (issued_phase & ~(1u << stage)) | (phase << stage);
+                    if (++stage == C::STAGES) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+            }
+            if (!ok) {
+                // Let every load still in flight land before shared memory is released.
+                const int zero = 0;
+                for (int s = 0; s < C::STAGES; s++)
+                    if ((issued_mask >> s) & 1u)
+                        if (!sm100::wait_parity_bounded(full_bar(s), (issued_phase >> s) & 1u, &zero,
+                                                        WAIT_BUDGET / 4))
+                            atomicOr(&g_device_status, 0x8u);
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            // ---------------- MMA issuer ----------------
+            constexpr uint32_t idesc = sm100::make_idesc_e2m3(BM, BN);
+            int stage = 0;
+            uint32_t phase = 0, acc_phase = 0;
+            bool ok = true, issued = false;
+            for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
+                const TileCoord tc = decode_tile(t, p);
+                if (!sm100::wait_parity_bounded(acc_empty, acc_phase ^ 1u, abort_flag, WAIT_BUDGET)) {
+                    if (!*abort_flag) raise_status(0x2u, abort_flag);
+                    ok = false;
+                    break;
+                }
+                sm100::tc_fence_after();
+                for (int i = 0; i < tc.kb_count; i++) {
+                    if (!sm100::wait_parity_bounded(full_bar(stage), phase, abort_flag, WAIT_BUDGET)) {
+                        if (!*abort_flag) raise_status(0x2u, abort_flag);
+                        ok = false;
+                        break;
+                    }
+                    sm100::tc_fence_after();
+                    const uint32_t sf_src = sf_base + stage * C::SF_STAGE;
+                    sm100::tc_cp_32x128b_warpx4(tmem_base + C::TMEM_SFA, sm100::make_sf_desc(sf_src));
+#pragma unroll
+                    for (int j = 0; j < C::SFB_ATOMS; j++)
+                        sm100::tc_cp_32x128b_warpx4(tmem_base + C::TMEM_SFB + 4 * j,
+                                                    sm100::make_sf_desc(sf_src + 512 + 512 * j));
+                    const uint32_t a_src = ab_base + stage * C::AB_STAGE;
+                    const uint32_t b_src = a_src + C::A_BYTES;
+#pragma unroll
+                    for (int k = 0; k < BK / 32; k++) {
+                        const uint64_t adesc = sm100::make_kmajor_sw128_desc(a_src + 32 * k);
+                        const uint64_t bdesc = sm100::make_kmajor_sw128_desc(b_src + 32 * k);
+                        const uint32_t sel = (uint32_t)k << 30;
+                        sm100::tc_mma_mxf8f6f4(tmem_base, adesc, bdesc,
+                                               sm100::idesc_with_sf_ids(idesc, k, k),
+                                               (tmem_base + C::TMEM_SFA) | sel,
+                                               (tmem_base + C::TMEM_SFB) | sel, (i > 0 || k > 0) ? 1u : 0u);
+                    }
+                    issued = true;
+                    sm100::tc_commit(empty_bar(stage));
+                    if (++stage == C::STAGES) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+                if (!ok) break;
+                sm100::tc_commit(acc_full);
+                acc_phase ^= 1u;
+            }
+            if (!ok && issued) {
+                // Wait for every MMA and copy already issued before tensor memory is freed.
+                const int zero = 0;
+                sm100::tc_commit(drain_bar);
+                if (!sm100::wait_parity_bounded(drain_bar, 0, &zero, WAIT_BUDGET / 4))
+                    atomicOr(&g_device_status, 0x8u);
+            }
+        }
+    } else {
+        // ---------------- epilogue (warps 2..5) ----------------
+        const int quarter = warp & 3;  // tensor-memory lanes 32*quarter .. 32*quarter+31
+        const uint32_t t_row = tmem_base + ((uint32_t)(32 * quarter) << 16);
+        uint32_t acc_phase = 0;
+        for (int t = blockIdx.x; t < total_tiles; t += gridDim.x) {
+            const TileCoord tc = decode_tile(t, p);
+            if (!sm100::wait_parity_bounded(acc_full, acc_phase, abort_flag, WAIT_BUDGET)) {
+                if (!*abort_flag) raise_status(0x4u, abort_flag);
+                break;
+            }
+            sm100::tc_fence_after();
+            const int row = tc.mb * BM + 32 * quarter + lane;
+            const int col0 = tc.nb * BN;
+#pragma unroll 1
+            for (int c = 0; c < BN; c += 32) {
+                if (col0 + c >= p.N) break;  // masked half tile (uniform across the warp)
+                uint32_t r[32];
+                sm100::tmem_ld_32x32b_x32(t_row + (uint32_t)c, r);
+                sm100::tmem_ld_wait();
+                if (row < p.M) {
+                    if constexpr (PARTIAL) {
+                        float* dst = p.ws + ((size_t)tc.split * p.M + row) * p.N + col0 + c;
+                        store_row_chunk<float>(dst, r);
+                    } else {
+                        OutT* dst = static_cast<OutT*>(p.D) + (size_t)row * p.N + col0 + c;
+                        store_row_chunk<OutT>(dst, r);
+                    }
+                }
+            }
+            sm100::tc_fence_before();
+            sm100::mbar_arrive(acc_empty);
+            acc_phase ^= 1u;
+        }
+    }
+
+    sm100::tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        __syncwarp();
+        sm100::tc_fence_after();
+        sm100::tmem_dealloc(tmem_base, C::TMEM_COLS);
+    }
+}
+
+// Split-K second stage (reference: src/kernel.hpp:305-313): D = sum_{s=0..S-1} ws[s], in that
+// fixed order, converted once. Four elements per thread per step (M*N % 4 == 0 always holds).
+template <typename OutT>
+__global__ void __launch_bounds__(256) reduce_partials(const float* __restrict__ ws, OutT* __restrict__ D,
+                                                       long long total, int S) {
+    const long long n4 = total / 4;
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n4;
+         i += (long long)gridDim.x * blockDim.x) {
+        float4 acc = reinterpret_cast<const float4*>(ws)[i];
+        for (int s = 1; s < S; s++) {
+            const float4 v = reinterpret_cast<const float4*>(ws + (size_t)s * total)[i];
+            acc.x += v.x;
+            acc.y += v.y;
+            acc.z += v.z;
+            acc.w += v.w;
+        }
+        if constexpr (std::is_same<OutT, float>::value) {
+            reinterpret_cast<float4*>(D)[i] = acc;
+        } else if constexpr (std::is_same<OutT, __half>::value) {
+            __half2 lo = __floats2half2_rn(acc.x, acc.y), hi = __floats2half2_rn(acc.z, acc.w);
+            uint2 o = make_uint2(*reinterpret_cast<uint32_t*>(&lo), *reinterpret_cast<uint32_t*>(&hi));
+            reinterpret_cast<uint2*>(D)[i] = o;
+        } else {
+            __nv_bfloat162 lo = __floats2bfloat162_rn(acc.x, acc.y),
+                           hi = __floats2bfloat162_rn(acc.z, acc.w);
+            uint2 o = make_uint2(*reinterpret_cast<uint32_t*>(&lo), *reinterpret_cast<uint32_t*>(&hi));
+            reinterpret_cast<uint2*>(D)[i] = o;
+        }
+    }
+}
+
+}  // namespace kern
+}  // namespace mxfp6

@@ -1,0 +1,225 @@
+"""Python binding of libmxfp6gemm (B200 MXFP6 GEMM) over its C ABI (include/mxfp6_gemm.h).
+
+Mirrors the reference library's public interface (eeezio/mxfp6-gemm include/mxfp6/gemm.hpp and
+include/mxfp6/preprocess.hpp): OutType, K_TILE, kpad, choose_tile, gemm_workspace_size, gemm,
+and the host layout producers quantize_to_mxfp6 / preprocess_B / preprocess_scale /
+preshuffle_B / tile_scale. Device buffers are passed as raw addresses (ints) or as objects with
+a data_ptr() method (torch tensors); the binding itself has no torch dependency.
+
+There is no CPU fallback: importing this module loads the compiled library and raises if it
+is missing, and every GEMM runs the sm_100a kernels.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import enum
+import os
+from dataclasses import dataclass
+
+import numpy as np
+
+PKG_DIR = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+LIB_PATH = os.path.join(PKG_DIR, "lib", "libmxfp6gemm.so")
+
+if not os.path.exists(LIB_PATH):
+    raise ImportError(f"{LIB_PATH} is missing: build it with `make -C {PKG_DIR}` "
+                      "(or python -c 'import __graft_entry__; __graft_entry__.build()')")
+
+_lib = C.CDLL(LIB_PATH)
+
+_u8p = np.ctypeslib.ndpointer(np.uint8, flags="C_CONTIGUOUS")
+_f32p = np.ctypeslib.ndpointer(np.float32, flags="C_CONTIGUOUS")
+
+
+def _fn(name, res, args):
+    f = getattr(_lib, name)
+    f.restype = res
+    f.argtypes = args
+    return f
+
+
+_gemm = _fn("mxfp6_gemm", None, [C.c_int, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p,
+                                 C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_void_p,
+                                 C.c_size_t])
+_gemm_stream = _fn("mxfp6_gemm_stream", None,
+                   [C.c_int, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p,
+                    C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_size_t, C.c_void_p])
+_force = _fn("mxfp6_gemm_force_tile", None,
+             [C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p,
+              C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_size_t,
+              C.c_void_p])
+_ws = _fn("mxfp6_gemm_workspace_size", C.c_size_t, [C.c_int, C.c_int, C.c_int])
+_choose = _fn("mxfp6_choose_tile", None, [C.c_int, C.c_int, C.c_int, C.POINTER(C.c_int)])
+_k_tile = _fn("mxfp6_k_tile", C.c_int, [])
+_kpad = _fn("mxfp6_kpad", C.c_int, [C.c_int])
+last_error = _fn("mxfp6_last_error", C.c_int, [])
+_last_error_string = _fn("mxfp6_last_error_string", C.c_char_p, [])
+_device_status = _fn("mxfp6_device_status", C.c_int, [])
+launch_count = _fn("mxfp6_launch_count", C.c_uint64, [])
+_quantize = _fn("mxfp6_quantize", None, [_f32p, C.c_int, C.c_int, _u8p, _u8p, C.c_int])
+_dequantize = _fn("mxfp6_dequantize", None, [_u8p, _u8p, C.c_int, C.c_int, _f32p])
+_tiled_bytes = _fn("mxfp6_tiled_scale_bytes", C.c_size_t, [C.c_int, C.c_int])
+_tile = _fn("mxfp6_tile_scales", None, [_u8p, C.c_int, C.c_int, _u8p])
+_untile = _fn("mxfp6_untile_scales", None, [_u8p, C.c_int, C.c_int, _u8p])
+_probe = _fn("mxfp6_probe_tma_fp6", C.c_int,
+             [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_uint32, C.c_void_p])
+
+# status codes (enum mxfp6_status)
+OK, ERR_INVALID_SHAPE, ERR_INVALID_STRIDE, ERR_MISALIGNED, ERR_NULL_POINTER = 0, 1, 2, 3, 4
+ERR_INVALID_OUT_TYPE, ERR_CUDA, ERR_DEVICE_TIMEOUT, ERR_WORKSPACE, ERR_UNSUPPORTED = 5, 6, 7, 8, 9
+
+
+class OutType(enum.IntEnum):
+    F32 = 0
+    F16 = 1
+    BF16 = 2
+
+
+K_TILE = _k_tile()
+
+
+def kpad(K: int) -> int:
+    return _kpad(K)
+
+
+@dataclass(frozen=True)
+class TileChoice:
+    MT: int
+    NT: int
+    MPW: int
+    NPW: int
+
+
+def choose_tile(M: int, N: int, Kp: int) -> TileChoice:
+    out = (C.c_int * 4)()
+    _choose(M, N, Kp, out)
+    return TileChoice(*out)
+
+
+def gemm_workspace_size(M: int, N: int, Kp: int) -> int:
+    return _ws(M, N, Kp)
+
+
+def _addr(x) -> int:
+    if x is None:
+        return 0
+    if isinstance(x, int):
+        return x
+    return int(x.data_ptr())
+
+
+def gemm(ot, M, N, Kp, dA, dBsh, dsA, dsB, dD, A_row_bytes, B_row_bytes, ws=None, ws_bytes=0,
+         stream=None):
+    """D[M,N] = A[M,K]·B[K,N] (mxfp6::gemm). Asynchronous; check last_error() after the call."""
+    args = (int(ot), M, N, Kp, _addr(dA), _addr(dBsh), _addr(dsA), _addr(dsB), _addr(dD),
+            A_row_bytes, B_row_bytes, _addr(ws), ws_bytes)
+    if stream is None:
+        _gemm(*args)
+    else:
+        _gemm_stream(*args, _addr(stream) if not hasattr(stream, "cuda_stream") else stream.cuda_stream)
+
+
+def gemm_force_tile(ot, M, N, Kp, NT, splits, dA, dBsh, dsA, dsB, dD, A_row_bytes, B_row_bytes,
+                    ws=None, ws_bytes=0, stream=None):
+    """Test hook (reference: gemm_force_tile): run tile width NT with `splits` K segments."""
+    s = 0 if stream is None else (stream.cuda_stream if hasattr(stream, "cuda_stream") else _addr(stream))
+    _force(int(ot), M, N, Kp, NT, splits, _addr(dA), _addr(dBsh), _addr(dsA), _addr(dsB), _addr(dD),
+           A_row_bytes, B_row_bytes, _addr(ws), ws_bytes, s)
+
+
+def last_error_string() -> str:
+    return _last_error_string().decode()
+
+
+def device_status() -> int:
+    """Synchronise and return (then clear) the kernels' sticky status bits; -1 if sync failed."""
+    return _device_status()
+
+
+def probe_tma_fp6(dsrc, rows, Kp, row_bytes, swizzle128, expect_bytes, dout) -> int:
+    return _probe(_addr(dsrc), rows, Kp, row_bytes, int(swizzle128), expect_bytes, _addr(dout))
+
+
+# ---- host layout producers (C++ header helpers through the C ABI) --------------------------------
+
+@dataclass
+class QuantizedMatrix:
+    packed_data: np.ndarray  # uint8 [rows][packed_row_bytes]
+    scales: np.ndarray       # uint8 [rows][cols/32]
+    rows: int
+    cols: int
+
+    @property
+    def packed_row_bytes(self) -> int:
+        return self.cols * 3 // 4
+
+    @property
+    def scale_cols(self) -> int:
+        return self.cols // 32
+
+
+def quantize_to_mxfp6(mat: np.ndarray, threads: int = 0) -> QuantizedMatrix:
+    mat = np.ascontiguousarray(mat, dtype=np.float32)
+    rows, cols = mat.shape
+    if cols % 32:
+        raise ValueError("cols must be a multiple of 32")
+    packed = np.empty((rows, cols * 3 // 4), np.uint8)
+    scales = np.empty((rows, cols // 32), np.uint8)
+    _quantize(mat, rows, cols, packed, scales, threads)
+    return QuantizedMatrix(packed, scales, rows, cols)
+
+
+def dequantize_mxfp6(q: QuantizedMatrix) -> np.ndarray:
+    out = np.empty((q.rows, q.cols), np.float32)
+    _dequantize(np.ascontiguousarray(q.packed_data), np.ascontiguousarray(q.scales), q.rows, q.cols, out)
+    return out
+
+
+def preprocess_B(B: np.ndarray, threads: int = 0) -> QuantizedMatrix:
+    """B[K][N] -> quantised B^T[N][K]."""
+    return quantize_to_mxfp6(np.ascontiguousarray(np.asarray(B, np.float32).T), threads)
+
+
+def preshuffle_B(Bq: QuantizedMatrix) -> np.ndarray:
+    """Identity on B200: the kernel reads B^T packed rows directly."""
+    return Bq.packed_data
+
+
+def tiled_scale_bytes(rows: int, cols: int) -> int:
+    return _tiled_bytes(rows, cols)
+
+
+def preprocess_scale(scales: np.ndarray, dim: int, K: int) -> np.ndarray:
+    """Raw scales [dim][K/32] -> B200 atom layout (also what tile_scale returns)."""
+    scales = np.ascontiguousarray(scales, dtype=np.uint8)
+    out = np.empty(tiled_scale_bytes(dim, K), np.uint8)
+    _tile(scales.reshape(-1), dim, K, out)
+    return out
+
+
+def tile_scale(ps: np.ndarray, group: int = 0, subs: int = 0) -> np.ndarray:
+    """The atom layout is route independent; kept for the reference's call shape."""
+    return ps
+
+
+def untile_scales(tiled: np.ndarray, dim: int, K: int) -> np.ndarray:
+    out = np.empty((dim, K // 32), np.uint8)
+    _untile(np.ascontiguousarray(tiled, dtype=np.uint8), dim, K, out.reshape(-1))
+    return out
+
+
+def pack_codes(codes: np.ndarray) -> np.ndarray:
+    """Pack 6-bit codes (last axis, length % 4 == 0) four per three bytes, LSB first."""
+    c = np.asarray(codes, dtype=np.uint32) & 63
+    g = c.reshape(c.shape[:-1] + (-1, 4))
+    w = g[..., 0] | (g[..., 1] << 6) | (g[..., 2] << 12) | (g[..., 3] << 18)
+    out = np.stack([w & 255, (w >> 8) & 255, (w >> 16) & 255], axis=-1).astype(np.uint8)
+    return out.reshape(c.shape[:-1] + (-1,))
+
+
+def unpack_codes(packed: np.ndarray) -> np.ndarray:
+    p = np.asarray(packed, dtype=np.uint32)
+    g = p.reshape(p.shape[:-1] + (-1, 3))
+    w = g[..., 0] | (g[..., 1] << 8) | (g[..., 2] << 16)
+    out = np.stack([(w >> (6 * i)) & 63 for i in range(4)], axis=-1).astype(np.uint8)
+    return out.reshape(p.shape[:-1] + (-1,))

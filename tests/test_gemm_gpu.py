@@ -1,0 +1,206 @@
+"""GPU parity: the sm_100a kernels through the C ABI against the CPU oracle.
+
+Cases mirror the reference's correctness list (tests/test_gemm.cpp:402-442 of eeezio/mxfp6-gemm)
+re-expressed for the B200 routes, for every output type, plus the BASELINE configurations
+(full-size, checked on sampled rows with the full K and N), determinism, poisoned outputs and
+the split-K workspace contract.
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+OUTS = ["F32", "F16", "BF16"]
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _cuda():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    torch.cuda.init()
+
+
+def _setup(M, N, K, kind="uniform", seed=None, **kw):
+    from mxfp6_b200.synth import make_operands
+    from gpu_helpers import DeviceOperands
+    seed = seed if seed is not None else M * 3 + N * 7 + K
+    ops = make_operands(M, N, K, kind=kind, seed=seed, **kw)
+    return ops, DeviceOperands(ops)
+
+
+def _ref(oracle, ops, rows=None):
+    return oracle.gemm(ops.A, ops.sA, ops.Bt, ops.sB, ops.Kp, rows=rows)
+
+
+def test_probe_tma_fp6_unpack_layout(lib):
+    """Pins the 16U6 unpack: 16 packed codes (12 bytes) per 16-byte shared-memory slot, in the
+    reference's packing order, 128-byte swizzle by row, and the byte count the load reports."""
+    rows, Kp = 128, 128
+    rng = np.random.default_rng(5)
+    src = rng.integers(0, 256, (rows, 96), dtype=np.uint8)
+    dsrc = torch.from_numpy(src).cuda()
+    results = {}
+    for swz in (0, 1):
+        for expect in (12288, 16384):
+            out = torch.zeros(rows * 128 + 16, dtype=torch.uint8, device="cuda")
+            assert lib.probe_tma_fp6(dsrc, rows, Kp, 96, swz, expect, out) == 0
+            torch.cuda.synchronize()
+            o = out.cpu().numpy()
+            flag = int(o[rows * 128:rows * 128 + 4].view(np.int32)[0])
+            results[(swz, expect)] = (flag, o[:rows * 128].reshape(rows, 128))
+            if flag:
+                break
+    flags = {k: v[0] for k, v in results.items()}
+    assert flags.get((0, 12288)) == 1, f"completion flags by (swizzle, expect_tx): {flags}"
+    for swz in (0, 1):
+        dump = results[(swz, 12288)][1]
+        for r in range(rows):
+            for j in range(8):
+                pos = (j ^ (r % 8)) if swz else j
+                slot = dump[r, 16 * pos:16 * pos + 12]
+                assert np.array_equal(slot, src[r, 12 * j:12 * j + 12]), f"swizzle={swz} row {r} slot {j}"
+
+
+def test_cfg1_256x256x512_fp32(lib, oracle):
+    """uniform codes over all 64 E2M3 values, exponents in [120, 134]."""
+    from gpu_helpers import check, run_gemm
+    ops, dev = _setup(256, 256, 512, kind="codes", seed=1, exp_range=(120, 134))
+    D = run_gemm(dev, lib.OutType.F32)
+    check(D, _ref(oracle, ops), lib.OutType.F32, oracle, label="cfg1")
+
+
+@pytest.mark.parametrize("ot", OUTS)
+@pytest.mark.parametrize("M,N,K", [(512, 512, 768), (768, 1280, 960), (4096, 4096, 768)])
+def test_reference_verify_cases(lib, oracle, ot, M, N, K):
+    from gpu_helpers import check, run_gemm
+    ops, dev = _setup(M, N, K)
+    D = run_gemm(dev, lib.OutType[ot])
+    check(D, _ref(oracle, ops), lib.OutType[ot], oracle, label=f"{M}x{N}x{K}")
+
+
+@pytest.mark.parametrize("ot", OUTS)
+@pytest.mark.parametrize("M,N,K,NT", [(256, 256, 768, 128), (384, 512, 1536, 128), (256, 384, 768, 256),
+                                      (384, 768, 960, 256), (1280, 1152, 384, 256), (128, 128, 128, 128),
+                                      (128, 256, 128, 256)])
+def test_forced_tiles(lib, oracle, ot, M, N, K, NT):
+    """Each tile width on small shapes (reference: verify_128x128 / verify_128x384), including
+    N % 256 == 128 under the 256-wide tile (masked half tile) and a single K slab."""
+    from gpu_helpers import check, run_gemm
+    ops, dev = _setup(M, N, K)
+    D = run_gemm(dev, lib.OutType[ot], force=(NT, 1))
+    check(D, _ref(oracle, ops), lib.OutType[ot], oracle, label=f"{M}x{N}x{K} NT={NT}")
+
+
+@pytest.mark.parametrize("ot", OUTS)
+@pytest.mark.parametrize("M,N,K,NT,S", [(2048, 1024, 12288, 256, 4), (2048, 1024, 3808, 256, 2),
+                                        (2048, 1024, 6400, 256, 3), (256, 384, 4096, 128, 5),
+                                        (512, 640, 1920, 256, 7)])
+def test_forced_splits(lib, oracle, ot, M, N, K, NT, S):
+    """Split-K with even and uneven segments (reference: verify_compact split cases) and the
+    deterministic FP32 reduce, for every output type."""
+    from gpu_helpers import check, run_gemm, sample_rows
+    ops, dev = _setup(M, N, K)
+    D = run_gemm(dev, lib.OutType[ot], force=(NT, S))
+    rows = sample_rows(M, 96) if M * N * ops.Kp > 2**31 else None
+    check(D, _ref(oracle, ops, rows), lib.OutType[ot], oracle, rows=rows, label=f"{M}x{N}x{K} S={S}")
+
+
+@pytest.mark.parametrize("M,N,K", [(128, 384, 3072), (256, 384, 32768), (512, 640, 960), (256, 1408, 384),
+                                   (2048, 1024, 12288)])
+def test_routed_shapes(lib, oracle, M, N, K):
+    """Routed (not forced) shapes from the reference's list, with and without a workspace."""
+    from gpu_helpers import check, run_gemm, sample_rows
+    ops, dev = _setup(M, N, K)
+    rows = sample_rows(M, 64) if M * N * ops.Kp > 2**31 else None
+    ref = _ref(oracle, ops, rows)
+    for ws_mode in ("sized", "none"):
+        D = run_gemm(dev, lib.OutType.F32, ws_mode=ws_mode)
+        check(D, ref, lib.OutType.F32, oracle, rows=rows, label=f"{M}x{N}x{K} ws={ws_mode}")
+
+
+def test_deterministic_and_split_invariant_bits(lib):
+    """Two runs give identical bits, with and without split-K."""
+    from gpu_helpers import run_gemm
+    ops, dev = _setup(1024, 768, 4096, kind="codes", seed=9)
+    for force in ((256, 1), (256, 3), (128, 4)):
+        a = run_gemm(dev, lib.OutType.F32, force=force)
+        b = run_gemm(dev, lib.OutType.F32, force=force)
+        assert torch.equal(a.view(torch.int32), b.view(torch.int32)), force
+
+
+def test_special_scales(lib, oracle):
+    """Scale code 255 (NaN) poisons exactly its rows / columns; code 0 (2^-127) and large codes stay finite."""
+    from gpu_helpers import DeviceOperands, check, run_gemm
+    from mxfp6_b200.synth import make_operands
+    ops = make_operands(256, 256, 512, kind="codes", seed=4, exp_range=(120, 134))
+    ops.sA[3, 2] = 255
+    ops.sB[17, 0] = 255
+    ops.sA[10, :] = 0
+    ops.sB[40, :] = 160
+    D = run_gemm(DeviceOperands(ops), lib.OutType.F32)
+    ref = _ref(oracle, ops)
+    check(D, ref, lib.OutType.F32, oracle, label="special scales")
+    g = D.numpy()
+    assert np.isnan(g[3]).all() and np.isnan(g[:, 17]).all()
+
+
+def test_row_permutation_and_scale_doubling(lib):
+    """Size-independent properties on a full-size shape: bumping every A scale exponent by one
+    doubles D exactly, and permuting A's rows permutes D's rows bit for bit."""
+    from gpu_helpers import DeviceOperands, run_gemm
+    from mxfp6_b200.synth import make_operands
+    ops = make_operands(2048, 2048, 4096, kind="codes", seed=12, exp_range=(118, 126))
+    D0 = run_gemm(DeviceOperands(ops), lib.OutType.F32)
+    ops.sA = ops.sA + 1
+    D1 = run_gemm(DeviceOperands(ops), lib.OutType.F32)
+    assert torch.equal(D1, D0 * 2)
+    ops.sA = ops.sA - 1
+    perm = np.random.default_rng(1).permutation(2048)
+    ops.A, ops.sA = ops.A[perm].copy(), ops.sA[perm].copy()
+    D2 = run_gemm(DeviceOperands(ops), lib.OutType.F32)
+    assert torch.equal(D2.view(torch.int32), D0[torch.from_numpy(perm)].view(torch.int32))
+
+
+@pytest.mark.parametrize("cfg", ["cfg2_square_f16_inrange", "cfg2_square_f16_overflow", "cfg3_narrow_deepk_f16",
+                                 "cfg4_wide_bf16", "cfg5_ffn_bf16"])
+def test_baseline_configs_sampled(lib, oracle, cfg):
+    """BASELINE configs 2-5 at full size; the oracle runs the full K and N on sampled rows."""
+    from gpu_helpers import check, run_gemm, sample_rows
+    spec = {
+        "cfg2_square_f16_inrange": (8192, 8192, 8192, "codes", (109, 127), lib.OutType.F16),
+        "cfg2_square_f16_overflow": (8192, 8192, 8192, "codes", (118, 136), lib.OutType.F16),
+        "cfg3_narrow_deepk_f16": (2048, 1024, 105728, "codes", (109, 127), lib.OutType.F16),
+        "cfg4_wide_bf16": (2048, 6144, 16128, "codes", (118, 136), lib.OutType.BF16),
+        "cfg5_ffn_bf16": (4096, 28672, 8192, "normal", None, lib.OutType.BF16),
+    }[cfg]
+    M, N, K, kind, er, ot = spec
+    kw = {"exp_range": er} if er else {}
+    ops, dev = _setup(M, N, K, kind=kind, seed=2026, **kw)
+    rows = sample_rows(M, 24)
+    D = run_gemm(dev, ot)
+    check(D, _ref(oracle, ops, rows), ot, oracle, rows=rows, label=cfg)
+
+
+def test_small_workspace_falls_back_unsplit(lib, oracle, capfd):
+    """A shape that wants split-K but gets too small a workspace runs unsplit, warns, and is right."""
+    from gpu_helpers import check, run_gemm, sample_rows
+    M, N, K = 2048, 1024, 12288
+    assert lib.gemm_workspace_size(M, N, K) > 0
+    ops, dev = _setup(M, N, K)
+    D = run_gemm(dev, lib.OutType.F32, ws_mode="none")
+    assert "split-K skipped" in capfd.readouterr().err
+    rows = sample_rows(M, 32)
+    check(D, _ref(oracle, ops, rows), lib.OutType.F32, oracle, rows=rows, label="ws fallback")
+
+
+def test_launch_counter_and_stream(lib, oracle):
+    from gpu_helpers import check, run_gemm
+    ops, dev = _setup(256, 512, 1024)
+    n0 = lib.launch_count()
+    s = torch.cuda.Stream()
+    D = run_gemm(dev, lib.OutType.F16, stream=s)
+    assert lib.launch_count() > n0
+    check(D, _ref(oracle, ops), lib.OutType.F16, oracle, label="stream")
