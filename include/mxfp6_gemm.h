@@ -74,10 +74,11 @@ void mxfp6_choose_tile(int M, int N, int Kp, int* out4);
 int mxfp6_k_tile(void);
 int mxfp6_kpad(int K);
 
-/* Test hook (reference: src/gemm.cpp:89-107 gemm_force_tile): run a specific tile width and
- * split factor instead of the routed one. NT in {128, 256}; splits >= 1 (splits > 1 needs
- * ws_bytes >= splits*M*N*4). Same validation as mxfp6_gemm; stream may be NULL. */
-void mxfp6_gemm_force_tile(int ot, int M, int N, int Kp, int NT, int splits, const void* dA,
+/* Test hook (reference: src/gemm.cpp:89-107 gemm_force_tile): run a specific tile and split
+ * factor instead of the routed one. (MT, NT) in {(256,256) CTA pair, (128,256), (128,128)};
+ * splits >= 1 (splits > 1 needs ws_bytes >= splits*M*N*4). Same validation as mxfp6_gemm;
+ * stream may be NULL. */
+void mxfp6_gemm_force_tile(int ot, int M, int N, int Kp, int MT, int NT, int splits, const void* dA,
                            const void* dBsh, const uint8_t* dsA, const uint8_t* dsB, void* dD,
                            int A_row_bytes, int B_row_bytes, void* ws, size_t ws_bytes,
                            void* stream);
@@ -92,6 +93,13 @@ int mxfp6_device_status(void);
 
 /* Number of kernels this library has launched in this process (all devices). */
 uint64_t mxfp6_launch_count(void);
+
+/* Diagnostic (no counterpart in the reference): one tensor-memory-accelerator load of a
+ * 128-element x `rows` box of packed FP6 (16U6 unpack mode, optional 128-byte swizzle) into
+ * shared memory, reported to an mbarrier that expects `expect_bytes`; the shared-memory box
+ * (rows*128 bytes) and a completion flag (int) are written to dout. Returns an mxfp6_status. */
+int mxfp6_probe_tma_fp6(const void* dsrc, int rows, int Kp, int row_bytes, int swizzle128,
+                        uint32_t expect_bytes, void* dout);
 
 /* ---- host preprocessing (C face of include/mxfp6/preprocess.hpp) --------------------------
  * All buffers are host memory, caller-allocated. Sizes: packed row = 3*cols/4 bytes,

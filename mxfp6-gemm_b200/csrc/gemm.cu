@@ -16,6 +16,7 @@
 #include <mutex>
 
 #include "gemm_kernel.cuh"
+#include "gemm_kernel_pair.cuh"
 #include "mxfp6/gemm.hpp"
 #include "mxfp6_gemm.h"
 #include "route.hpp"
@@ -98,6 +99,22 @@ bool make_fp6_tmap(CUtensorMap* map, const void* ptr, int rows, int Kp, int row_
     CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_16U6_ALIGN16B, 2, const_cast<void*>(ptr), dims,
                     strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
+// Tiled scales viewed as [row_atoms][k_slabs][128 x u32] (512-byte atoms), read one or two
+// atoms at a time; atoms past the last row block read as zero.
+bool make_sf_tmap(CUtensorMap* map, const void* ptr, int rows, int Kp, int box_atoms) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return false;
+    const int k_slabs = Kp / 128, atoms = (rows + 127) / 128;
+    cuuint64_t dims[3] = {128u, (cuuint64_t)k_slabs, (cuuint64_t)atoms};
+    cuuint64_t strides[2] = {512u, (cuuint64_t)k_slabs * 512u};
+    cuuint32_t box[3] = {128u, 1u, (cuuint32_t)box_atoms};
+    cuuint32_t estr[3] = {1u, 1u, 1u};
+    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT32, 3, const_cast<void*>(ptr), dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS;
 }
 
@@ -193,6 +210,68 @@ bool launch_gemm(int M, int N, int Kp, const void* dA, const void* dB, const uin
     return true;
 }
 
+template <typename OutT, bool PARTIAL>
+bool launch_pair(int M, int N, int Kp, const void* dA, const void* dB, const uint8_t* sA, const uint8_t* sB,
+                 void* dD, float* ws, int A_row_bytes, int B_row_bytes, int splits, cudaStream_t stream) {
+    using C = kern::PairConfig;
+    auto kernel = kern::gemm_mxfp6_sm100_pair<OutT, PARTIAL>;
+    static std::once_flag attr_once[kMaxDevices];
+    const int dev = current_device();
+    if (dev < 0 || dev >= kMaxDevices) {
+        set_error(MXFP6_ERR_CUDA, "no CUDA device");
+        return false;
+    }
+    cudaError_t attr_err = cudaSuccess;
+    std::call_once(attr_once[dev], [&] {
+        attr_err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
+    });
+    if (attr_err != cudaSuccess) {
+        set_error(MXFP6_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(attr_err));
+        return false;
+    }
+    CUtensorMap tmA, tmB, tmSA, tmSB;
+    if (!make_fp6_tmap(&tmA, dA, M, Kp, A_row_bytes, 128) || !make_fp6_tmap(&tmB, dB, N, Kp, B_row_bytes, 128) ||
+        !make_sf_tmap(&tmSA, sA, M, Kp, 1) || !make_sf_tmap(&tmSB, sB, N, Kp, 2)) {
+        set_error(MXFP6_ERR_CUDA, "cuTensorMapEncodeTiled failed for %dx%dx%d", M, N, Kp);
+        return false;
+    }
+    kern::Params p;
+    p.sfA = sA;
+    p.sfB = sB;
+    p.D = dD;
+    p.ws = ws;
+    p.M = M;
+    p.N = N;
+    p.Kp = Kp;
+    p.m_blocks = (M + C::BM - 1) / C::BM;
+    p.n_blocks = (N + C::BN - 1) / C::BN;
+    p.k_slabs = Kp / kern::BK;
+    p.splits = splits;
+    const long long units = (long long)p.m_blocks * p.n_blocks * splits;
+    const int pairs = sm_count() / 2;
+    const int clusters = (int)(units < pairs ? units : pairs);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * clusters, 1, 1);
+    cfg.blockDim = dim3(kern::NUM_THREADS, 1, 1);
+    cfg.dynamicSmemBytes = C::SMEM_BYTES;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, tmA, tmB, tmSA, tmSB, p);
+    if (e == cudaSuccess) e = cudaGetLastError();
+    if (e != cudaSuccess) {
+        set_error(MXFP6_ERR_CUDA, "pair GEMM launch failed: %s", cudaGetErrorString(e));
+        return false;
+    }
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+    return true;
+}
+
 template <typename OutT>
 bool launch_reduce(const float* ws, void* dD, int M, int N, int splits, cudaStream_t stream) {
     const long long total = (long long)M * N;
@@ -211,28 +290,33 @@ bool launch_reduce(const float* ws, void* dD, int M, int N, int splits, cudaStre
 }
 
 template <typename OutT>
-bool run_typed(int M, int N, int Kp, int NT, int splits, const void* dA, const void* dB,
-               const uint8_t* sA, const uint8_t* sB, void* dD, int Ar, int Br, void* ws,
-               cudaStream_t stream) {
+bool run_typed(const Route& r, int M, int N, int Kp, const void* dA, const void* dB, const uint8_t* sA,
+               const uint8_t* sB, void* dD, int Ar, int Br, void* ws, cudaStream_t stream) {
     float* wsf = static_cast<float*>(ws);
-    if (splits > 1) {
-        bool ok = NT == 256 ? launch_gemm<256, OutT, true>(M, N, Kp, dA, dB, sA, sB, dD, wsf, Ar, Br, splits, stream)
-                            : launch_gemm<128, OutT, true>(M, N, Kp, dA, dB, sA, sB, dD, wsf, Ar, Br, splits, stream);
-        return ok && launch_reduce<OutT>(wsf, dD, M, N, splits, stream);
+    const bool part = r.splits > 1;
+    bool ok;
+    if (r.MT == 256) {
+        ok = part ? launch_pair<OutT, true>(M, N, Kp, dA, dB, sA, sB, dD, wsf, Ar, Br, r.splits, stream)
+                  : launch_pair<OutT, false>(M, N, Kp, dA, dB, sA, sB, dD, wsf, Ar, Br, 1, stream);
+    } else if (r.NT == 256) {
+        ok = part ? launch_gemm<256, OutT, true>(M, N, Kp, dA, dB, sA, sB, dD, wsf, Ar, Br, r.splits, stream)
+                  : launch_gemm<256, OutT, false>(M, N, Kp, dA, dB, sA, sB, dD, wsf, Ar, Br, 1, stream);
+    } else {
+        ok = part ? launch_gemm<128, OutT, true>(M, N, Kp, dA, dB, sA, sB, dD, wsf, Ar, Br, r.splits, stream)
+                  : launch_gemm<128, OutT, false>(M, N, Kp, dA, dB, sA, sB, dD, wsf, Ar, Br, 1, stream);
     }
-    return NT == 256 ? launch_gemm<256, OutT, false>(M, N, Kp, dA, dB, sA, sB, dD, wsf, Ar, Br, 1, stream)
-                     : launch_gemm<128, OutT, false>(M, N, Kp, dA, dB, sA, sB, dD, wsf, Ar, Br, 1, stream);
+    return ok && (!part || launch_reduce<OutT>(wsf, dD, M, N, r.splits, stream));
 }
 
-bool run(int ot, int M, int N, int Kp, int NT, int splits, const void* dA, const void* dB,
-         const uint8_t* sA, const uint8_t* sB, void* dD, int Ar, int Br, void* ws, cudaStream_t stream) {
+bool run(int ot, const Route& r, int M, int N, int Kp, const void* dA, const void* dB, const uint8_t* sA,
+         const uint8_t* sB, void* dD, int Ar, int Br, void* ws, cudaStream_t stream) {
     switch (ot) {
         case MXFP6_OUT_F32:
-            return run_typed<float>(M, N, Kp, NT, splits, dA, dB, sA, sB, dD, Ar, Br, ws, stream);
+            return run_typed<float>(r, M, N, Kp, dA, dB, sA, sB, dD, Ar, Br, ws, stream);
         case MXFP6_OUT_F16:
-            return run_typed<__half>(M, N, Kp, NT, splits, dA, dB, sA, sB, dD, Ar, Br, ws, stream);
+            return run_typed<__half>(r, M, N, Kp, dA, dB, sA, sB, dD, Ar, Br, ws, stream);
         default:
-            return run_typed<__nv_bfloat16>(M, N, Kp, NT, splits, dA, dB, sA, sB, dD, Ar, Br, ws, stream);
+            return run_typed<__nv_bfloat16>(r, M, N, Kp, dA, dB, sA, sB, dD, Ar, Br, ws, stream);
     }
 }
 
@@ -253,7 +337,7 @@ void gemm_entry(int ot, int M, int N, int Kp, const void* dA, const void* dB, co
             r.splits = 1;
         }
     }
-    run(ot, M, N, Kp, r.NT, r.splits, dA, dB, sA, sB, dD, Ar, Br, ws, stream);
+    run(ot, r, M, N, Kp, dA, dB, sA, sB, dD, Ar, Br, ws, stream);
 }
 
 }  // namespace
@@ -262,7 +346,7 @@ void gemm_entry(int ot, int M, int N, int Kp, const void* dA, const void* dB, co
 
 TileChoice choose_tile(int M, int N, int Kp) {
     Route r = route_for(M, N, Kp, sm_count());
-    return TileChoice{128, r.NT, 128 / 32, r.NT / 32};
+    return TileChoice{r.MT, r.NT, r.MT / 32, r.NT / 32};
 }
 
 size_t gemm_workspace_size(int M, int N, int Kp) {
@@ -318,14 +402,15 @@ int mxfp6_kpad(int K) {
     return kpad(K);
 }
 
-void mxfp6_gemm_force_tile(int ot, int M, int N, int Kp, int NT, int splits, const void* dA,
+void mxfp6_gemm_force_tile(int ot, int M, int N, int Kp, int MT, int NT, int splits, const void* dA,
                            const void* dBsh, const uint8_t* dsA, const uint8_t* dsB, void* dD,
                            int A_row_bytes, int B_row_bytes, void* ws, size_t ws_bytes,
                            void* stream) {
     t_last_error = MXFP6_OK;
     if (!validate(ot, M, N, Kp, dA, dBsh, dsA, dsB, dD, A_row_bytes, B_row_bytes)) return;
-    if ((NT != 128 && NT != 256) || splits < 1 || splits > Kp / K_TILE) {
-        set_error(MXFP6_ERR_UNSUPPORTED, "forced route NT=%d splits=%d not available for Kp=%d", NT,
+    const bool tile_ok = (MT == 256 && NT == 256) || (MT == 128 && (NT == 128 || NT == 256));
+    if (!tile_ok || splits < 1 || splits > Kp / K_TILE) {
+        set_error(MXFP6_ERR_UNSUPPORTED, "forced route %dx%d splits=%d not available for Kp=%d", MT, NT,
                   splits, Kp);
         return;
     }
@@ -334,7 +419,7 @@ void mxfp6_gemm_force_tile(int ot, int M, int N, int Kp, int NT, int splits, con
                   splitk_bytes(M, N, splits), ws_bytes);
         return;
     }
-    run(ot, M, N, Kp, NT, splits, dA, dBsh, dsA, dsB, dD, A_row_bytes, B_row_bytes, ws,
+    run(ot, Route{MT, NT, splits}, M, N, Kp, dA, dBsh, dsA, dsB, dD, A_row_bytes, B_row_bytes, ws,
         static_cast<cudaStream_t>(stream));
 }
 

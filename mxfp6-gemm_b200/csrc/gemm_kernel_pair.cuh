@@ -1,0 +1,292 @@
+#pragma once
+// The B200 MXFP6 GEMM kernel for large shapes: a CTA pair (cluster of 2, tcgen05 cta_group::2)
+// computes a 256 x 256 output tile with one MMA stream.
+//
+// Same math as gemm_mxfp6_sm100 (gemm_kernel.cuh); the pair layout halves what each SM stages:
+//   * CTA r of the pair loads A rows [m0 + 128r, +128) and B^T rows [n0 + 128r, +128) of every
+//     128-deep K slab (16U6 unpack, 128-byte swizzle), its own A scale atom and both B scale
+//     atoms (tensor loads with zero fill past the edges), into a 6-stage ring; all loads of both
+//     CTAs report to the leader's (rank 0) full barrier.
+//   * The leader's MMA thread copies the scale atoms into each CTA's tensor memory and issues
+//     tcgen05.mma.cta_group::2 (M = 256, N = 256, K = 32) four times per slab; each CTA's tensor
+//     memory receives its 128 rows x 256 FP32 columns. tcgen05.commit multicasts slot releases
+//     and "accumulator ready" to both CTAs.
+//   * Two accumulators share tensor memory with a 32-column overlap: buffer 0 = columns [0,256),
+//     buffer 1 = [224,480), scales at [480,492). The epilogue reads buffer 0 from its top chunk
+//     down and buffer 1 from its bottom chunk up, so the overlap chunk is read first and the
+//     next tile's MMAs may start as soon as that one chunk has left tensor memory; the rest of
+//     the epilogue runs under the next tile's main loop.
+//   * No TMA multicast anywhere: each CTA fetches its own operands.
+// Every wait is bounded (see gemm_kernel.cuh); a timeout also raises the peer's abort flag.
+#include "gemm_kernel.cuh"
+
+namespace mxfp6 {
+namespace kern {
+
+struct PairConfig {
+    static constexpr int BM = 256;  // rows per pair tile (128 per CTA)
+    static constexpr int BN = 256;  // columns per pair tile (B rows 128 per CTA)
+    static constexpr int STAGES = 6;
+    static constexpr int A_BYTES = 128 * BK;
+    static constexpr int B_BYTES = 128 * BK;
+    static constexpr int AB_STAGE = A_BYTES + B_BYTES;
+    static constexpr int SF_STAGE = 512 + 1024;  // own A atom, both B atoms
+    static constexpr uint32_t TX_PER_CTA = 2 * (128 * BK * 3 / 4) + 512 + 1024;
+    static constexpr uint32_t TX_STAGE = 2 * TX_PER_CTA;  // leader's barrier counts both CTAs
+    static constexpr int TMEM_COLS = 512;
+    static constexpr int BUF1_COL = 224;  // buffer 1 starts 32 columns below buffer 0's end
+    static constexpr int TMEM_SFA = 480;
+    static constexpr int TMEM_SFB = 484;
+    static constexpr int EPI_WARPS = 4;
+    static constexpr int BAR_BYTES = 256;
+    static constexpr int SMEM_BYTES = 1024 + STAGES * (AB_STAGE + SF_STAGE) + BAR_BYTES;
+    static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
+};
+
+__device__ __forceinline__ void store_cluster_u32(uint32_t cluster_addr, uint32_t v) {
+    asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(cluster_addr), "r"(v) : "memory");
+}
+
+// Spin for about `ns` nanoseconds (bounded settle time on the abort path).
+__device__ __forceinline__ void settle_ns(unsigned long long ns) {
+    unsigned long long t0, t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+    do {
+        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    } while (t - t0 < ns);
+}
+
+template <typename OutT, bool PARTIAL>
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    gemm_mxfp6_sm100_pair(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                          const __grid_constant__ CUtensorMap tmSA, const __grid_constant__ CUtensorMap tmSB,
+                          const Params p) {
+    using C = PairConfig;
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    const uint32_t raw_u32 = sm100::smem_u32(smem_raw);
+    const uint32_t base = (raw_u32 + 1023u) & ~1023u;
+    uint8_t* base_ptr = smem_raw + (base - raw_u32);
+
+    const uint32_t ab_base = base;
+    const uint32_t sf_base = base + C::STAGES * C::AB_STAGE;
+    const uint32_t bar_base = sf_base + C::STAGES * C::SF_STAGE;
+    uint8_t* bar_ptr = base_ptr + (bar_base - base);
+    // barriers: full[S], empty[S], acc_full[2], acc_empty[2], ovl_free, drain
+    auto full_bar = [&](int s) { return bar_base + 8u * s; };
+    auto empty_bar = [&](int s) { return bar_base + 8u * (C::STAGES + s); };
+    const uint32_t acc_full0 = bar_base + 8u * (2 * C::STAGES);
+    const uint32_t acc_empty0 = acc_full0 + 16u;
+    const uint32_t ovl_free = acc_full0 + 32u;
+    const uint32_t drain_bar = acc_full0 + 40u;
+    const int slot_off = 8 * (2 * C::STAGES + 6);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_ptr + slot_off);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(bar_ptr + slot_off + 8);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const uint32_t rank = sm100::cluster_ctarank();
+    const uint32_t peer = rank ^ 1u;
+    const uint32_t peer_abort = sm100::mapa_shared(sm100::smem_u32((const void*)abort_flag), peer);
+    auto raise = [&](unsigned int bit) {
+        atomicOr(&g_device_status, bit);
+        *abort_flag = 1;
+        store_cluster_u32(peer_abort, 1);
+    };
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < C::STAGES; s++) {
+            sm100::mbar_init(full_bar(s), 1);
+            sm100::mbar_init(empty_bar(s), 1);
+        }
+        for (int b = 0; b < 2; b++) {
+            sm100::mbar_init(acc_full0 + 8u * b, 1);
+            sm100::mbar_init(acc_empty0 + 8u * b, 2 * C::EPI_WARPS);
+        }
+        sm100::mbar_init(ovl_free, 2 * C::EPI_WARPS);
+        sm100::mbar_init(drain_bar, 1);
+        *abort_flag = 0;
+        sm100::fence_mbar_init();
+        sm100::fence_async_shared();
+        sm100::prefetch_tmap(&tmA);
+        sm100::prefetch_tmap(&tmB);
+        sm100::prefetch_tmap(&tmSA);
+        sm100::prefetch_tmap(&tmSB);
+    }
+    if (warp == 1) {
+        sm100::tmem_alloc_pair(sm100::smem_u32(tmem_slot), C::TMEM_COLS);
+        sm100::tmem_relinquish_pair();
+    }
+    sm100::tc_fence_before();
+    __syncthreads();
+    sm100::cluster_sync();  // the peer's loads and arrivals target barriers initialised above
+    sm100::tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    const int total_tiles = p.m_blocks * p.n_blocks * p.splits;
+    const int cluster_id = blockIdx.x >> 1;
+    const int num_clusters = gridDim.x >> 1;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            // ---------------- TMA producer (both CTAs) ----------------
+            int stage = 0;
+            uint32_t phase = 0;
+            uint32_t issued_mask = 0, issued_phase = 0;
+            bool ok = true;
+            for (int t = cluster_id; t < total_tiles && ok; t += num_clusters) {
+                const TileCoord tc = decode_tile(t, p);
+                const int a_row = tc.mb * C::BM + 128 * (int)rank;
+                const int b_row = tc.nb * C::BN + 128 * (int)rank;
+                for (int i = 0; i < tc.kb_count; i++) {
+                    if (!sm100::wait_parity_bounded_cluster(empty_bar(stage), phase ^ 1u, abort_flag, WAIT_BUDGET)) {
+                        if (!*abort_flag) raise(0x1u);
+                        ok = false;
+                        break;
+                    }
+                    const int kb = tc.kb_begin + i;
+                    const uint32_t fb = sm100::mapa_shared(full_bar(stage), 0);
+                    if (rank == 0) sm100::mbar_arrive_expect_tx(full_bar(stage), C::TX_STAGE);
+                    const uint32_t a_dst = ab_base + stage * C::AB_STAGE;
+                    sm100::tma_load_2d_pair(a_dst, &tmA, fb, kb * BK, a_row);
+                    sm100::tma_load_2d_pair(a_dst + C::A_BYTES, &tmB, fb, kb * BK, b_row);
+                    const uint32_t sf_dst = sf_base + stage * C::SF_STAGE;
+                    sm100::tma_load_3d_pair(sf_dst, &tmSA, fb, 0, kb, tc.mb * 2 + (int)rank);
+                    sm100::tma_load_3d_pair(sf_dst + 512, &tmSB, fb, 0, kb, tc.nb * 2);
+                    issued_mask |= 1u << stage;
+                    issued_phase = (issued_phase & ~(1u << stage)) | (phase << stage);
+                    if (++stage == C::STAGES) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+            }
+            if (!ok) {
+                const int zero = 0;
+                if (rank == 0) {
+                    for (int s = 0; s < C::STAGES; s++)
+                        if ((issued_mask >> s) & 1u)
+                            if (!sm100::wait_parity_bounded_cluster(full_bar(s), (issued_phase >> s) & 1u, &zero,
+                                                                    WAIT_BUDGET / 4))
+                                atomicOr(&g_device_status, 0x8u);
+                } else {
+                    settle_ns(200000);  // the peer's loads report to the leader; give them time to land
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0 && rank == 0) {
+            // ---------------- MMA issuer (leader only) ----------------
+            constexpr uint32_t idesc = sm100::make_idesc_e2m3(C::BM, C::BN);
+            int stage = 0;
+            uint32_t phase = 0;
+            bool ok = true, issued = false;
+            int local = 0;
+            for (int t = cluster_id; t < total_tiles && ok; t += num_clusters, local++) {
+                const TileCoord tc = decode_tile(t, p);
+                const int b = local & 1;
+                const uint32_t d_col = b ? C::BUF1_COL : 0;
+                if (!sm100::wait_parity_bounded_cluster(acc_empty0 + 8u * b, ((local >> 1) & 1) ^ 1u, abort_flag,
+                                                        WAIT_BUDGET) ||
+                    (local >= 1 && !sm100::wait_parity_bounded_cluster(ovl_free, (local - 1) & 1, abort_flag,
+                                                                       WAIT_BUDGET))) {
+                    if (!*abort_flag) raise(0x2u);
+                    ok = false;
+                    break;
+                }
+                sm100::tc_fence_after();
+                for (int i = 0; i < tc.kb_count; i++) {
+                    if (!sm100::wait_parity_bounded_cluster(full_bar(stage), phase, abort_flag, WAIT_BUDGET)) {
+                        if (!*abort_flag) raise(0x2u);
+                        ok = false;
+                        break;
+                    }
+                    sm100::tc_fence_after();
+                    const uint32_t sf_src = sf_base + stage * C::SF_STAGE;
+                    sm100::tc_cp_32x128b_warpx4_pair(tmem_base + C::TMEM_SFA, sm100::make_sf_desc(sf_src));
+                    sm100::tc_cp_32x128b_warpx4_pair(tmem_base + C::TMEM_SFB, sm100::make_sf_desc(sf_src + 512));
+                    sm100::tc_cp_32x128b_warpx4_pair(tmem_base + C::TMEM_SFB + 4, sm100::make_sf_desc(sf_src + 1024));
+                    const uint32_t a_src = ab_base + stage * C::AB_STAGE;
+                    const uint32_t b_src = a_src + C::A_BYTES;
+#pragma unroll
+                    for (int k = 0; k < BK / 32; k++) {
+                        const uint32_t sel = (uint32_t)k << 30;
+                        sm100::tc_mma_mxf8f6f4_pair(tmem_base + d_col, sm100::make_kmajor_sw128_desc(a_src + 32 * k),
+                                                    sm100::make_kmajor_sw128_desc(b_src + 32 * k),
+                                                    sm100::idesc_with_sf_ids(idesc, k, k),
+                                                    (tmem_base + C::TMEM_SFA) | sel, (tmem_base + C::TMEM_SFB) | sel,
+                                                    (i > 0 || k > 0) ? 1u : 0u);
+                    }
+                    issued = true;
+                    sm100::tc_commit_pair(empty_bar(stage), 0x3);
+                    if (++stage == C::STAGES) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+                if (!ok) break;
+                sm100::tc_commit_pair(acc_full0 + 8u * b, 0x3);
+            }
+            if (!ok && issued) {
+                const int zero = 0;
+                sm100::tc_commit_pair(drain_bar, 0x1);
+                if (!sm100::wait_parity_bounded_cluster(drain_bar, 0, &zero, WAIT_BUDGET / 4))
+                    atomicOr(&g_device_status, 0x8u);
+            }
+        }
+    } else {
+        // ---------------- epilogue (warps 2..5 of both CTAs) ----------------
+        const int quarter = warp & 3;
+        const uint32_t t_lane = tmem_base + ((uint32_t)(32 * quarter) << 16);
+        const uint32_t leader_acc_empty = sm100::mapa_shared(acc_empty0, 0);
+        const uint32_t leader_ovl_free = sm100::mapa_shared(ovl_free, 0);
+        int local = 0;
+        for (int t = cluster_id; t < total_tiles; t += num_clusters, local++) {
+            const TileCoord tc = decode_tile(t, p);
+            const int b = local & 1;
+            if (!sm100::wait_parity_bounded_cluster(acc_full0 + 8u * b, (local >> 1) & 1, abort_flag, WAIT_BUDGET)) {
+                if (!*abort_flag) raise(0x4u);
+                break;
+            }
+            sm100::tc_fence_after();
+            const int row = tc.mb * C::BM + 128 * (int)rank + 32 * quarter + lane;
+            const int col0 = tc.nb * C::BN;
+#pragma unroll 1
+            for (int j = 0; j < C::BN / 32; j++) {
+                // buffer 0 top-down, buffer 1 bottom-up: the shared chunk [224, 256) goes first
+                const int c = b ? j : (C::BN / 32 - 1 - j);
+                const uint32_t tcol = (b ? C::BUF1_COL : 0) + 32 * c;
+                uint32_t r[32];
+                sm100::tmem_ld_32x32b_x32(t_lane + tcol, r);
+                sm100::tmem_ld_wait();
+                if (j == 0) {
+                    sm100::tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) sm100::mbar_arrive_cluster(leader_ovl_free);
+                }
+                const int col = col0 + 32 * c;
+                if (row < p.M && col < p.N) {
+                    if constexpr (PARTIAL) {
+                        store_row_chunk<float>(p.ws + ((size_t)tc.split * p.M + row) * p.N + col, r);
+                    } else {
+                        store_row_chunk<OutT>(static_cast<OutT*>(p.D) + (size_t)row * p.N + col, r);
+                    }
+                }
+            }
+            sm100::tc_fence_before();
+            __syncwarp();
+            if (lane == 0) sm100::mbar_arrive_cluster(leader_acc_empty + 8u * b);
+        }
+    }
+
+    sm100::tc_fence_before();
+    __syncthreads();
+    sm100::cluster_sync();  // no CTA leaves while its peer may still touch its shared memory
+    if (warp == 1) {
+        __syncwarp();
+        sm100::tc_fence_after();
+        sm100::tmem_dealloc_pair(tmem_base, C::TMEM_COLS);
+    }
+}
+
+}  // namespace kern
+}  // namespace mxfp6

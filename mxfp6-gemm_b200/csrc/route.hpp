@@ -1,26 +1,32 @@
 #pragma once
-// Route selection for the B200 kernel (host only, no CUDA dependency).
+// Route selection for the B200 kernels (host only, no CUDA dependency).
 //
 // Reference counterpart: choose_tile (src/gemm.cpp:12-59) and splitk_S (src/dispatch.hpp:30-53),
 // which pick among four gfx950 tiles from a 256-CU wave table. Here the choice is re-derived
-// for B200: the kernel has 128-row tiles of width NT in {128, 256} and an optional split of K
-// into S segments (FP32 partials in the caller's workspace plus one reduce pass). A small cost
-// model estimates each candidate's time on `sms` SMs:
+// for B200 over three tiles,
+//   256 x 256  CTA pair (cluster of 2, tcgen05 cta_group::2), 74 pairs on 148 SMs
+//   128 x 256  single CTA
+//   128 x 128  single CTA
+// and an optional split of K into S segments (FP32 partials in the caller's workspace plus one
+// reduce pass). A cost model estimates each candidate's time on `sms` SMs:
 //
-//   waves   = ceil(tiles * S / sms)                      persistent CTAs take tiles round-robin
-//   mainloop= waves * ceil(slabs / S) * w * T_SLAB       one 128-deep K slab of a 128x256 tile
-//   tile    = waves * T_TILE * w                         epilogue + pipeline fill per tile
-//             (w = 1 for NT = 256, 0.6 for NT = 128)
-//   splitk  = (2*S + 1) * M*N*4 / HBM                    partial write + reduce read + D write
+//   units   = ceil(M/MT) * ceil(N/NT) * S              work items handed out round-robin
+//   waves   = ceil(units / (sms / ctas_per_unit))      persistent CTAs (or pairs) take units
+//   time    = waves * (ceil(slabs / S) * T_slab + T_tile)   one slab = 128-deep K step
+//           + (2S + 1) * M*N*4 / HBM  when S > 1        partial write + reduce read + D write
 //
-// and takes the cheapest (ties: fewer splits, then the wider tile). gemm_workspace_size() and
+// T_slab is the time one SM (or pair) spends per slab: 256x256 and 128x256 tiles do the same
+// MMA work per SM per slab; their constants reflect how well each keeps the tensor pipe fed
+// (measured: the pair sustains more, the narrow tile pays for streaming A at half the work).
+// The cheapest candidate wins (a later candidate must win by 3%). gemm_workspace_size() and
 // gemm() both call route_for(), so the workspace a caller sizes always matches what is used.
 #include <cstddef>
 
 namespace mxfp6 {
 
 struct Route {
-    int NT;      // tile width (columns of D per tile)
+    int MT;      // tile rows: 256 = CTA pair, 128 = single CTA
+    int NT;      // tile columns
     int splits;  // K segments (1 = no split)
 };
 
@@ -28,37 +34,50 @@ inline size_t splitk_bytes(int M, int N, int splits) {
     return (size_t)splits * (size_t)M * (size_t)N * sizeof(float);
 }
 
-inline double route_cost_us(int M, int N, int Kp, int NT, int S, int sms) {
-    const double T_SLAB = 0.28;   // us: 4 x (128x256x32) MMAs at about 1.9 GHz
-    const double T_TILE = 0.8;    // us: per-tile epilogue and ramp for a 256-wide tile
-    const double HBM = 6.5e6;     // bytes per us
-    const long long tiles = (long long)(M / 128) * ((N + NT - 1) / NT) * S;
-    const long long waves = (tiles + sms - 1) / sms;
+inline double route_cost_us(int M, int N, int Kp, int MT, int NT, int S, int sms) {
+    const double HBM = 6.5e6;  // bytes per us
+    double t_slab, t_tile;
+    int per_unit;
+    if (MT == 256) {
+        t_slab = 0.30;  // us per 128-deep slab of a 256x256 pair tile (4 MMAs of 128x256 per SM)
+        t_tile = 0.3;
+        per_unit = 2;
+    } else if (NT == 256) {
+        t_slab = 0.40;
+        t_tile = 1.0;
+        per_unit = 1;
+    } else {
+        t_slab = 0.24;
+        t_tile = 0.6;
+        per_unit = 1;
+    }
+    const long long units = (long long)((M + MT - 1) / MT) * ((N + NT - 1) / NT) * S;
+    const long long slots = sms / per_unit > 0 ? sms / per_unit : 1;
+    const long long waves = (units + slots - 1) / slots;
     const int slabs = Kp / 128;
     const int per = (slabs + S - 1) / S;
-    // A 128-wide tile halves the MMA work per slab but not the A traffic: each slab streams
-    // 32 KB through shared memory in 256 cycles, at the edge of its bandwidth; charge 0.6.
-    const double w = NT == 256 ? 1.0 : 0.6;
-    double t = (double)waves * (per * T_SLAB * w + T_TILE * w);
+    double t = (double)waves * (per * t_slab + t_tile);
     if (S > 1) t += (2.0 * S + 1.0) * (double)M * N * 4.0 / HBM;
     return t;
 }
 
 inline Route route_for(int M, int N, int Kp, int sms) {
-    Route best{N >= 256 ? 256 : 128, 1};
+    Route best{128, N >= 256 ? 256 : 128, 1};
     if (M <= 0 || N <= 0 || Kp < 128 || sms <= 0) return best;
     const int slabs = Kp / 128;
-    double best_t = route_cost_us(M, N, Kp, best.NT, 1, sms);
-    const int widths[2] = {256, 128};
-    for (int NT : widths) {
-        if (NT == 256 && N < 256) continue;
+    double best_t = route_cost_us(M, N, Kp, best.MT, best.NT, 1, sms);
+    const int shapes[3][2] = {{256, 256}, {128, 256}, {128, 128}};
+    bool first = true;
+    for (const auto& sh : shapes) {
+        const int MT = sh[0], NT = sh[1];
+        if (MT > 128 && sms < 2) continue;
         const int s_max = slabs / 4 < 32 ? slabs / 4 : 32;  // every segment keeps >= 4 slabs
         for (int S = 1; S <= (s_max > 1 ? s_max : 1); S++) {
-            double t = route_cost_us(M, N, Kp, NT, S, sms);
-            // a candidate must win by 3% to displace the simpler one found earlier
-            if (t < best_t * 0.97) {
+            const double t = route_cost_us(M, N, Kp, MT, NT, S, sms);
+            if (first || t < best_t * 0.97) {
                 best_t = t;
-                best = Route{NT, S};
+                best = Route{MT, NT, S};
+                first = false;
             }
         }
     }

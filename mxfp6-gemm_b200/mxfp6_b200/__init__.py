@@ -45,7 +45,7 @@ _gemm_stream = _fn("mxfp6_gemm_stream", None,
                    [C.c_int, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p,
                     C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_size_t, C.c_void_p])
 _force = _fn("mxfp6_gemm_force_tile", None,
-             [C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p,
+             [C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p,
               C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_size_t,
               C.c_void_p])
 _ws = _fn("mxfp6_gemm_workspace_size", C.c_size_t, [C.c_int, C.c_int, C.c_int])
@@ -119,11 +119,11 @@ def gemm(ot, M, N, Kp, dA, dBsh, dsA, dsB, dD, A_row_bytes, B_row_bytes, ws=None
         _gemm_stream(*args, _addr(stream) if not hasattr(stream, "cuda_stream") else stream.cuda_stream)
 
 
-def gemm_force_tile(ot, M, N, Kp, NT, splits, dA, dBsh, dsA, dsB, dD, A_row_bytes, B_row_bytes,
+def gemm_force_tile(ot, M, N, Kp, MT, NT, splits, dA, dBsh, dsA, dsB, dD, A_row_bytes, B_row_bytes,
                     ws=None, ws_bytes=0, stream=None):
-    """Test hook (reference: gemm_force_tile): run tile width NT with `splits` K segments."""
+    """Test hook (reference: gemm_force_tile): run tile MT x NT with `splits` K segments."""
     s = 0 if stream is None else (stream.cuda_stream if hasattr(stream, "cuda_stream") else _addr(stream))
-    _force(int(ot), M, N, Kp, NT, splits, _addr(dA), _addr(dBsh), _addr(dsA), _addr(dsB), _addr(dD),
+    _force(int(ot), M, N, Kp, MT, NT, splits, _addr(dA), _addr(dBsh), _addr(dsA), _addr(dsB), _addr(dD),
            A_row_bytes, B_row_bytes, _addr(ws), ws_bytes, s)
 
 

@@ -29,14 +29,14 @@ class DeviceOperands:
 
 
 def run_gemm(dev: DeviceOperands, ot, ws_mode="sized", force=None, poison=True, stream=None):
-    """Run the routed GEMM (or a forced route (NT, splits)); returns D as a torch CPU tensor."""
+    """Run the routed GEMM (or a forced route (MT, NT, splits)); returns D as a torch CPU tensor."""
     o = dev.ops
     D = torch.empty((o.M, o.N), dtype=TORCH_OUT[ot], device=dev.A.device)
     if poison:
         D.view(torch.uint8).fill_(0x5A)
     ws, wsb = None, 0
     if force is not None:
-        NT, S = force
+        MT, NT, S = force
         if S > 1:
             wsb = S * o.M * o.N * 4
     elif ws_mode == "sized":
@@ -51,7 +51,7 @@ def run_gemm(dev: DeviceOperands, ot, ws_mode="sized", force=None, poison=True, 
         lib.gemm(ot, o.M, o.N, o.Kp, dev.A, dev.Bt, dev.sA, dev.sB, D, o.row_bytes, o.row_bytes, ws, wsb,
                  stream=stream)
     else:
-        lib.gemm_force_tile(ot, o.M, o.N, o.Kp, force[0], force[1], dev.A, dev.Bt, dev.sA, dev.sB, D,
+        lib.gemm_force_tile(ot, o.M, o.N, o.Kp, force[0], force[1], force[2], dev.A, dev.Bt, dev.sA, dev.sB, D,
                             o.row_bytes, o.row_bytes, ws, wsb, stream=stream)
     err = lib.last_error()
     assert err == lib.OK, f"gemm rejected the call: {err} {lib.last_error_string()}"

@@ -82,28 +82,32 @@ def test_reference_verify_cases(lib, oracle, ot, M, N, K):
 
 
 @pytest.mark.parametrize("ot", OUTS)
-@pytest.mark.parametrize("M,N,K,NT", [(256, 256, 768, 128), (384, 512, 1536, 128), (256, 384, 768, 256),
-                                      (384, 768, 960, 256), (1280, 1152, 384, 256), (128, 128, 128, 128),
-                                      (128, 256, 128, 256)])
-def test_forced_tiles(lib, oracle, ot, M, N, K, NT):
-    """Each tile width on small shapes (reference: verify_128x128 / verify_128x384), including
-    N % 256 == 128 under the 256-wide tile (masked half tile) and a single K slab."""
+@pytest.mark.parametrize("M,N,K,MT,NT", [
+    (256, 256, 768, 128, 128), (384, 512, 1536, 128, 128), (256, 384, 768, 128, 256), (384, 768, 960, 128, 256),
+    (1280, 1152, 384, 128, 256), (128, 128, 128, 128, 128), (128, 256, 128, 128, 256),
+    (256, 256, 768, 256, 256), (512, 512, 1536, 256, 256), (384, 640, 960, 256, 256), (128, 128, 128, 256, 256),
+    (1280, 1152, 384, 256, 256), (2304, 2560, 1024, 256, 256)])
+def test_forced_tiles(lib, oracle, ot, M, N, K, MT, NT):
+    """Every tile on small shapes (reference: verify_128x128 / verify_128x384), including
+    partial tiles (M % 256 == 128 or N % 256 == 128: zero-filled loads, masked stores), a single
+    K slab, and more tiles than CTA pairs (persistent loop with both accumulator buffers)."""
     from gpu_helpers import check, run_gemm
     ops, dev = _setup(M, N, K)
-    D = run_gemm(dev, lib.OutType[ot], force=(NT, 1))
-    check(D, _ref(oracle, ops), lib.OutType[ot], oracle, label=f"{M}x{N}x{K} NT={NT}")
+    D = run_gemm(dev, lib.OutType[ot], force=(MT, NT, 1))
+    check(D, _ref(oracle, ops), lib.OutType[ot], oracle, label=f"{M}x{N}x{K} {MT}x{NT}")
 
 
 @pytest.mark.parametrize("ot", OUTS)
-@pytest.mark.parametrize("M,N,K,NT,S", [(2048, 1024, 12288, 256, 4), (2048, 1024, 3808, 256, 2),
-                                        (2048, 1024, 6400, 256, 3), (256, 384, 4096, 128, 5),
-                                        (512, 640, 1920, 256, 7)])
-def test_forced_splits(lib, oracle, ot, M, N, K, NT, S):
+@pytest.mark.parametrize("M,N,K,MT,NT,S", [(2048, 1024, 12288, 128, 256, 4), (2048, 1024, 3808, 128, 256, 2),
+                                           (2048, 1024, 6400, 128, 256, 3), (256, 384, 4096, 128, 128, 5),
+                                           (512, 640, 1920, 128, 256, 7), (2048, 1024, 12288, 256, 256, 4),
+                                           (2048, 1024, 6400, 256, 256, 3), (384, 640, 4096, 256, 256, 5)])
+def test_forced_splits(lib, oracle, ot, M, N, K, MT, NT, S):
     """Split-K with even and uneven segments (reference: verify_compact split cases) and the
     deterministic FP32 reduce, for every output type."""
     from gpu_helpers import check, run_gemm, sample_rows
     ops, dev = _setup(M, N, K)
-    D = run_gemm(dev, lib.OutType[ot], force=(NT, S))
+    D = run_gemm(dev, lib.OutType[ot], force=(MT, NT, S))
     rows = sample_rows(M, 96) if M * N * ops.Kp > 2**31 else None
     check(D, _ref(oracle, ops, rows), lib.OutType[ot], oracle, rows=rows, label=f"{M}x{N}x{K} S={S}")
 
@@ -125,7 +129,7 @@ def test_deterministic_and_split_invariant_bits(lib):
     """Two runs give identical bits, with and without split-K."""
     from gpu_helpers import run_gemm
     ops, dev = _setup(1024, 768, 4096, kind="codes", seed=9)
-    for force in ((256, 1), (256, 3), (128, 4)):
+    for force in ((128, 256, 1), (128, 256, 3), (128, 128, 4), (256, 256, 1), (256, 256, 3)):
         a = run_gemm(dev, lib.OutType.F32, force=force)
         b = run_gemm(dev, lib.OutType.F32, force=force)
         assert torch.equal(a.view(torch.int32), b.view(torch.int32)), force
@@ -187,7 +191,7 @@ def test_baseline_configs_sampled(lib, oracle, cfg):
 def test_small_workspace_falls_back_unsplit(lib, oracle, capfd):
     """A shape that wants split-K but gets too small a workspace runs unsplit, warns, and is right."""
     from gpu_helpers import check, run_gemm, sample_rows
-    M, N, K = 2048, 1024, 12288
+    M, N, K = 2048, 1024, 105728
     assert lib.gemm_workspace_size(M, N, K) > 0
     ops, dev = _setup(M, N, K)
     D = run_gemm(dev, lib.OutType.F32, ws_mode="none")

@@ -109,8 +109,8 @@ def test_route_covers_every_shape(lib):
         for M in range(128, 16385, 1024):
             for N in range(128, 24577, 640):
                 t = lib.choose_tile(M, N, Kp)
-                assert t.MT == 128 and t.NT in (128, 256) and M % t.MT == 0
-                assert N % t.NT == 0 or (t.NT == 256 and N % 128 == 0)
+                assert (t.MT, t.NT) in ((256, 256), (128, 256), (128, 128))
+                assert M % 128 == 0 and N % 128 == 0  # every tile covers the rest by masking
                 assert (t.MPW, t.NPW) == (t.MT // 32, t.NT // 32)
                 ws = lib.gemm_workspace_size(M, N, Kp)
                 assert ws % (M * N * 4) == 0
@@ -125,7 +125,8 @@ def test_route_examples(lib):
     assert lib.gemm_workspace_size(4096, 28672, 8192) == 0
     assert lib.gemm_workspace_size(2048, 1024, 105728) > 0
     assert lib.gemm_workspace_size(256, 256, 512) == 0
-    assert lib.choose_tile(128, 128, 128).NT == 128
+    assert lib.gemm_workspace_size(128, 128, 128) == 0
+    assert lib.choose_tile(8192, 8192, 8192).MT == 256  # CTA-pair tile on machine-filling shapes
 
 
 def test_workspace_query_on_degenerate_shapes(lib):
@@ -161,7 +162,9 @@ def test_invalid_arguments_rejected(lib, capfd, args, code):
 
 
 def test_forced_route_validation(lib, capfd):
-    lib.gemm_force_tile(0, 128, 128, 128, 192, 1, 0x1000, 0x2000, 0x3000, 0x4000, 0x5000, 96, 96)
+    lib.gemm_force_tile(0, 128, 128, 128, 128, 192, 1, 0x1000, 0x2000, 0x3000, 0x4000, 0x5000, 96, 96)
     assert lib.last_error() == lib.ERR_UNSUPPORTED
-    lib.gemm_force_tile(0, 128, 128, 512, 128, 2, 0x1000, 0x2000, 0x3000, 0x4000, 0x5000, 384, 384, None, 0)
+    lib.gemm_force_tile(0, 128, 128, 128, 256, 128, 1, 0x1000, 0x2000, 0x3000, 0x4000, 0x5000, 96, 96)
+    assert lib.last_error() == lib.ERR_UNSUPPORTED
+    lib.gemm_force_tile(0, 128, 128, 512, 128, 128, 2, 0x1000, 0x2000, 0x3000, 0x4000, 0x5000, 384, 384, None, 0)
     assert lib.last_error() == lib.ERR_WORKSPACE
