@@ -138,7 +138,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 const int a_row = tc.mb * C::BM + 128 * (int)rank;
                 const int b_row = tc.nb * C::BN + 128 * (int)rank;
                 for (int i = 0; i < tc.kb_count; i++) {
-                    if (!sm100::wait_parity_bounded_cluster(empty_bar(stage), phase ^ 1u, abort_flag, WAIT_BUDGET)) {
+                    if (!sm100::wait_parity_bounded(empty_bar(stage), phase ^ 1u, abort_flag, WAIT_BUDGET)) {
                         if (!*abort_flag) raise(0x1u);
                         ok = false;
                         break;
@@ -165,7 +165,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 if (rank == 0) {
                     for (int s = 0; s < C::STAGES; s++)
                         if ((issued_mask >> s) & 1u)
-                            if (!sm100::wait_parity_bounded_cluster(full_bar(s), (issued_phase >> s) & 1u, &zero,
+                            if (!sm100::wait_parity_bounded(full_bar(s), (issued_phase >> s) & 1u, &zero,
                                                                     WAIT_BUDGET / 4))
                                 atomicOr(&g_device_status, 0x8u);
                 } else {
@@ -177,6 +177,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         if (lane == 0 && rank == 0) {
             // ---------------- MMA issuer (leader only) ----------------
             constexpr uint32_t idesc = sm100::make_idesc_e2m3(C::BM, C::BN);
+            uint32_t idesc_k[BK / 32];
+#pragma unroll
+            for (int k = 0; k < BK / 32; k++) idesc_k[k] = sm100::idesc_with_sf_ids(idesc, k, k);
+            const uint64_t a_desc0 = sm100::make_kmajor_sw128_desc(ab_base);
+            const uint64_t b_desc0 = sm100::make_kmajor_sw128_desc(ab_base + C::A_BYTES);
+            const uint32_t sfa_t = tmem_base + C::TMEM_SFA;
+            const uint32_t sfb_t = tmem_base + C::TMEM_SFB;
             int stage = 0;
             uint32_t phase = 0;
             bool ok = true, issued = false;
@@ -184,37 +191,36 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             for (int t = cluster_id; t < total_tiles && ok; t += num_clusters, local++) {
                 const TileCoord tc = decode_tile(t, p);
                 const int b = local & 1;
-                const uint32_t d_col = b ? C::BUF1_COL : 0;
-                if (!sm100::wait_parity_bounded_cluster(acc_empty0 + 8u * b, ((local >> 1) & 1) ^ 1u, abort_flag,
+                const uint32_t d_taddr = tmem_base + (b ? C::BUF1_COL : 0);
+                if (!sm100::wait_parity_bounded(acc_empty0 + 8u * b, ((local >> 1) & 1) ^ 1u, abort_flag,
                                                         WAIT_BUDGET) ||
-                    (local >= 1 && !sm100::wait_parity_bounded_cluster(ovl_free, (local - 1) & 1, abort_flag,
+                    (local >= 1 && !sm100::wait_parity_bounded(ovl_free, (local - 1) & 1, abort_flag,
                                                                        WAIT_BUDGET))) {
                     if (!*abort_flag) raise(0x2u);
                     ok = false;
                     break;
                 }
                 sm100::tc_fence_after();
+                // The issuing thread keeps the tensor pipe's short queue fed: it polls the next
+                // slab's barrier without blocking right after issuing the current one, and
+                // blocks only when that slab's data has not landed yet.
+                bool ready = sm100::mbar_test_wait(full_bar(stage), phase);
                 for (int i = 0; i < tc.kb_count; i++) {
-                    if (!sm100::wait_parity_bounded_cluster(full_bar(stage), phase, abort_flag, WAIT_BUDGET)) {
+                    if (!ready && !sm100::wait_parity_bounded(full_bar(stage), phase, abort_flag, WAIT_BUDGET)) {
                         if (!*abort_flag) raise(0x2u);
                         ok = false;
                         break;
                     }
-                    sm100::tc_fence_after();
                     const uint32_t sf_src = sf_base + stage * C::SF_STAGE;
-                    sm100::tc_cp_32x128b_warpx4_pair(tmem_base + C::TMEM_SFA, sm100::make_sf_desc(sf_src));
-                    sm100::tc_cp_32x128b_warpx4_pair(tmem_base + C::TMEM_SFB, sm100::make_sf_desc(sf_src + 512));
-                    sm100::tc_cp_32x128b_warpx4_pair(tmem_base + C::TMEM_SFB + 4, sm100::make_sf_desc(sf_src + 1024));
-                    const uint32_t a_src = ab_base + stage * C::AB_STAGE;
-                    const uint32_t b_src = a_src + C::A_BYTES;
+                    sm100::tc_cp_32x128b_warpx4_pair(sfa_t, sm100::make_sf_desc(sf_src));
+                    sm100::tc_cp_32x128b_warpx4_pair(sfb_t, sm100::make_sf_desc(sf_src + 512));
+                    sm100::tc_cp_32x128b_warpx4_pair(sfb_t + 4, sm100::make_sf_desc(sf_src + 1024));
+                    const uint32_t off16 = (uint32_t)(stage * C::AB_STAGE) >> 4;  // descriptor address units
 #pragma unroll
                     for (int k = 0; k < BK / 32; k++) {
                         const uint32_t sel = (uint32_t)k << 30;
-                        sm100::tc_mma_mxf8f6f4_pair(tmem_base + d_col, sm100::make_kmajor_sw128_desc(a_src + 32 * k),
-                                                    sm100::make_kmajor_sw128_desc(b_src + 32 * k),
-                                                    sm100::idesc_with_sf_ids(idesc, k, k),
-                                                    (tmem_base + C::TMEM_SFA) | sel, (tmem_base + C::TMEM_SFB) | sel,
-                                                    (i > 0 || k > 0) ? 1u : 0u);
+                        sm100::tc_mma_mxf8f6f4_pair(d_taddr, a_desc0 + off16 + 2 * k, b_desc0 + off16 + 2 * k,
+                                                    idesc_k[k], sfa_t | sel, sfb_t | sel, (i > 0 || k > 0) ? 1u : 0u);
                     }
                     issued = true;
                     sm100::tc_commit_pair(empty_bar(stage), 0x3);
@@ -222,6 +228,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                         stage = 0;
                         phase ^= 1u;
                     }
+                    ready = sm100::mbar_test_wait(full_bar(stage), phase);
                 }
                 if (!ok) break;
                 sm100::tc_commit_pair(acc_full0 + 8u * b, 0x3);
@@ -229,7 +236,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             if (!ok && issued) {
                 const int zero = 0;
                 sm100::tc_commit_pair(drain_bar, 0x1);
-                if (!sm100::wait_parity_bounded_cluster(drain_bar, 0, &zero, WAIT_BUDGET / 4))
+                if (!sm100::wait_parity_bounded(drain_bar, 0, &zero, WAIT_BUDGET / 4))
                     atomicOr(&g_device_status, 0x8u);
             }
         }
@@ -243,7 +250,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         for (int t = cluster_id; t < total_tiles; t += num_clusters, local++) {
             const TileCoord tc = decode_tile(t, p);
             const int b = local & 1;
-            if (!sm100::wait_parity_bounded_cluster(acc_full0 + 8u * b, (local >> 1) & 1, abort_flag, WAIT_BUDGET)) {
+            if (!sm100::wait_parity_bounded(acc_full0 + 8u * b, (local >> 1) & 1, abort_flag, WAIT_BUDGET)) {
                 if (!*abort_flag) raise(0x4u);
                 break;
             }

@@ -51,6 +51,19 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
     return ok != 0;
 }
 
+// Non-blocking probe: has the phase with the given parity completed?
+__device__ __forceinline__ bool mbar_test_wait(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
 // Wait until the phase with the given parity has completed. Returns false when `budget` clock
 // cycles pass first, or as soon as *abort becomes non-zero (another role already gave up).
 __device__ __forceinline__ bool wait_parity_bounded(uint32_t bar, uint32_t parity,
@@ -78,6 +91,12 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const void* tmap, uint
         " [%0], [%1, {%3, %4}], [%2];" ::"r"(dst),
         "l"(tmap), "r"(bar), "r"(c0), "r"(c1)
         : "memory");
+}
+
+// Prefetch a 2-D box of a tensor map into L2 (no shared-memory destination, no completion).
+__device__ __forceinline__ void tma_prefetch_2d(const void* tmap, int c0, int c1) {
+    asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global [%0, {%1, %2}];" ::"l"(tmap), "r"(c0), "r"(c1)
+                 : "memory");
 }
 
 // Untiled bulk copy global -> shared (16-byte aligned addresses, size a multiple of 16).
