@@ -198,6 +198,7 @@ bool launch_gemm(int M, int N, int Kp, const void* dA, const void* dB, const uin
     p.n_blocks = (N + BN - 1) / BN;
     p.k_slabs = Kp / kern::BK;
     p.splits = splits;
+    p.out_align32 = aligned(PARTIAL ? static_cast<const void*>(ws) : dD, 32) ? 1 : 0;
     const long long tiles = (long long)p.m_blocks * p.n_blocks * splits;
     const int grid = (int)(tiles < sm_count() ? tiles : sm_count());
     kernel<<<grid, kern::NUM_THREADS, C::SMEM_BYTES, stream>>>(tmA, tmB, p);
@@ -247,6 +248,7 @@ bool launch_pair(int M, int N, int Kp, const void* dA, const void* dB, const uin
     p.n_blocks = (N + C::BN - 1) / C::BN;
     p.k_slabs = Kp / kern::BK;
     p.splits = splits;
+    p.out_align32 = aligned(PARTIAL ? static_cast<const void*>(ws) : dD, 32) ? 1 : 0;
     const long long units = (long long)p.m_blocks * p.n_blocks * splits;
     const int pairs = sm_count() / 2;
     const int clusters = (int)(units < pairs ? units : pairs);

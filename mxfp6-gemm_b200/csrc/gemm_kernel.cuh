@@ -77,6 +77,7 @@ struct Params {
     float* ws;           // FP32 partials [splits][M][N] in partial mode
     int M, N, Kp;
     int m_blocks, n_blocks, k_slabs, splits;
+    int out_align32;  // D (or ws in partial mode) is 32-byte aligned: 256-bit stores
 };
 
 struct TileCoord {
@@ -106,32 +107,48 @@ __device__ __forceinline__ void raise_status(unsigned int bit, volatile int* abo
     *abort_flag = 1;
 }
 
+// 32 consecutive outputs of one row from 32 FP32 accumulator words. With a 32-byte aligned
+// destination the stores are 256-bit (full L2 sectors), otherwise 128-bit.
+__device__ __forceinline__ void st_v8(void* dst, const uint32_t* w) {
+    asm volatile("st.global.v8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"l"(dst), "r"(w[0]), "r"(w[1]), "r"(w[2]),
+                 "r"(w[3]), "r"(w[4]), "r"(w[5]), "r"(w[6]), "r"(w[7])
+                 : "memory");
+}
+
+template <int NWORDS>
+__device__ __forceinline__ void store_words(void* dst, const uint32_t* w, bool align32) {
+    if (align32) {
+#pragma unroll
+        for (int i = 0; i < NWORDS / 8; i++) st_v8(static_cast<uint8_t*>(dst) + 32 * i, w + 8 * i);
+    } else {
+        uint4* d = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+        for (int i = 0; i < NWORDS / 4; i++) d[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+    }
+}
+
 template <typename OutT>
-__device__ __forceinline__ void store_row_chunk(OutT* dst, const uint32_t (&r)[32]);
+__device__ __forceinline__ void store_row_chunk(OutT* dst, const uint32_t (&r)[32], bool align32);
 
 template <>
-__device__ __forceinline__ void store_row_chunk<float>(float* dst, const uint32_t (&r)[32]) {
-    uint4* d = reinterpret_cast<uint4*>(dst);
-#pragma unroll
-    for (int i = 0; i < 8; i++) d[i] = make_uint4(r[4 * i], r[4 * i + 1], r[4 * i + 2], r[4 * i + 3]);
+__device__ __forceinline__ void store_row_chunk<float>(float* dst, const uint32_t (&r)[32], bool align32) {
+    store_words<32>(dst, r, align32);
 }
 
 template <>
-__device__ __forceinline__ void store_row_chunk<__half>(__half* dst, const uint32_t (&r)[32]) {
+__device__ __forceinline__ void store_row_chunk<__half>(__half* dst, const uint32_t (&r)[32], bool align32) {
     uint32_t h[16];
 #pragma unroll
     for (int i = 0; i < 16; i++) {
         __half2 v = __floats2half2_rn(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1]));
         h[i] = *reinterpret_cast<uint32_t*>(&v);
     }
-    uint4* d = reinterpret_cast<uint4*>(dst);
-#pragma unroll
-    for (int i = 0; i < 4; i++) d[i] = make_uint4(h[4 * i], h[4 * i + 1], h[4 * i + 2], h[4 * i + 3]);
+    store_words<16>(dst, h, align32);
 }
 
 template <>
-__device__ __forceinline__ void store_row_chunk<__nv_bfloat16>(__nv_bfloat16* dst,
-                                                               const uint32_t (&r)[32]) {
+__device__ __forceinline__ void store_row_chunk<__nv_bfloat16>(__nv_bfloat16* dst, const uint32_t (&r)[32],
+                                                               bool align32) {
     uint32_t h[16];
 #pragma unroll
     for (int i = 0; i < 16; i++) {
@@ -139,9 +156,7 @@ __device__ __forceinline__ void store_row_chunk<__nv_bfloat16>(__nv_bfloat16* ds
             __floats2bfloat162_rn(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1]));
         h[i] = *reinterpret_cast<uint32_t*>(&v);
     }
-    uint4* d = reinterpret_cast<uint4*>(dst);
-#pragma unroll
-    for (int i = 0; i < 4; i++) d[i] = make_uint4(h[4 * i], h[4 * i + 1], h[4 * i + 2], h[4 * i + 3]);
+    store_words<16>(dst, h, align32);
 }
 
 // OutT: float / __half / __nv_bfloat16. PARTIAL: write FP32 partial sums to p.ws instead of D.
@@ -330,10 +345,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 if (row < p.M) {
                     if constexpr (PARTIAL) {
                         float* dst = p.ws + ((size_t)tc.split * p.M + row) * p.N + col0 + c;
-                        store_row_chunk<float>(dst, r);
+                        store_row_chunk<float>(dst, r, p.out_align32 != 0);
                     } else {
                         OutT* dst = static_cast<OutT*>(p.D) + (size_t)row * p.N + col0 + c;
-                        store_row_chunk<OutT>(dst, r);
+                        store_row_chunk<OutT>(dst, r, p.out_align32 != 0);
                     }
                 }
             }

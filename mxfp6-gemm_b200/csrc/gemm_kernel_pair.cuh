@@ -273,9 +273,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 const int col = col0 + 32 * c;
                 if (row < p.M && col < p.N) {
                     if constexpr (PARTIAL) {
-                        store_row_chunk<float>(p.ws + ((size_t)tc.split * p.M + row) * p.N + col, r);
+                        store_row_chunk<float>(p.ws + ((size_t)tc.split * p.M + row) * p.N + col, r, p.out_align32 != 0);
                     } else {
-                        store_row_chunk<OutT>(static_cast<OutT*>(p.D) + (size_t)row * p.N + col, r);
+                        store_row_chunk<OutT>(static_cast<OutT*>(p.D) + (size_t)row * p.N + col, r, p.out_align32 != 0);
                     }
                 }
             }

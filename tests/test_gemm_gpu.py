@@ -208,3 +208,21 @@ def test_launch_counter_and_stream(lib, oracle):
     D = run_gemm(dev, lib.OutType.F16, stream=s)
     assert lib.launch_count() > n0
     check(D, _ref(oracle, ops), lib.OutType.F16, oracle, label="stream")
+
+
+@pytest.mark.parametrize("MT,NT", [(256, 256), (128, 256)])
+def test_output_only_16_byte_aligned(lib, oracle, MT, NT):
+    """D at a 16-byte (not 32-byte) aligned address takes the 128-bit store path."""
+    from gpu_helpers import check
+    ops, dev = _setup(256, 512, 1024)
+    o = ops
+    raw = torch.full((o.M * o.N * 2 + 64,), 0x5A, dtype=torch.uint8, device="cuda")
+    base = raw.data_ptr()
+    off = (32 - base % 32) % 32 + 16
+    D = raw[off:off + o.M * o.N * 2].view(torch.float16).view(o.M, o.N)
+    assert D.data_ptr() % 32 == 16
+    lib.gemm_force_tile(lib.OutType.F16, o.M, o.N, o.Kp, MT, NT, 1, dev.A, dev.Bt, dev.sA, dev.sB, D, o.row_bytes,
+                        o.row_bytes)
+    assert lib.last_error() == lib.OK
+    assert lib.device_status() == 0
+    check(D.cpu(), _ref(oracle, ops), lib.OutType.F16, oracle, label="16-byte aligned D")
