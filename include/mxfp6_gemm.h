@@ -83,6 +83,24 @@ void mxfp6_gemm_force_tile(int ot, int M, int N, int Kp, int MT, int NT, int spl
                            int A_row_bytes, int B_row_bytes, void* ws, size_t ws_bytes,
                            void* stream);
 
+/* No counterpart in the reference. The same computation as mxfp6_gemm_stream, for callers that
+ * cannot call cudaMalloc: for example a plugin inside a host application that owns every device
+ * allocation through its own pool, or a foreign-function binding that only forwards pointers it
+ * was given and has no way to create a workspace. Nothing is allocated: when the route splits K,
+ * the FP32 partial sums go to a fixed array inside this library (mxfp6_static_workspace_bytes(),
+ * 32 MiB), which every GPU that loads the library reserves until the process exits. A shape whose
+ * split needs more than that is rejected with MXFP6_ERR_WORKSPACE and nothing is launched.
+ * The first call on a device looks up the array's device address (cudaGetSymbolAddress) with
+ * that device current; make that first call before any stream capture. All calls share the one
+ * array and it keeps the last call's contents (every partial is written before it is read, so
+ * nothing needs clearing); calls that overlap on the GPU, on any streams, race on it. */
+void mxfp6_gemm_static_workspace(int ot, int M, int N, int Kp, const void* dA, const void* dBsh,
+                                 const uint8_t* dsA, const uint8_t* dsB, void* dD, int A_row_bytes,
+                                 int B_row_bytes, void* stream);
+
+/* Size in bytes of the static split-K array mxfp6_gemm_static_workspace uses. */
+size_t mxfp6_static_workspace_bytes(void);
+
 /* Status of the last mxfp6_* call on this thread, and a static message for it. */
 int mxfp6_last_error(void);
 const char* mxfp6_last_error_string(void);

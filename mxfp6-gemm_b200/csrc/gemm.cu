@@ -342,6 +342,29 @@ void gemm_entry(int ot, int M, int N, int Kp, const void* dA, const void* dB, co
     run(ot, r, M, N, Kp, dA, dB, sA, sB, dD, Ar, Br, ws, stream);
 }
 
+// ---- split-K scratch owned by the library (mxfp6_gemm_static_workspace) --------------------------------
+//
+// For callers that cannot allocate device memory themselves. The FP32 split-K partials go to
+// this fixed-size array instead of a caller workspace. It is an ordinary module global: every
+// device that loads this library reserves kStaticWorkspaceBytes for it until the process exits.
+// Host code must not hand `g_static_split_ws` to a kernel directly (on the host the name is a
+// stand-in, not a device address); its device address is looked up once per device with
+// cudaGetSymbolAddress, with that device current, on the first call made there.
+constexpr size_t kStaticWorkspaceBytes = size_t(32) << 20;
+static __device__ __align__(256) unsigned char g_static_split_ws[kStaticWorkspaceBytes];
+void* g_static_ws_addr[kMaxDevices];
+cudaError_t g_static_ws_err[kMaxDevices];
+std::once_flag g_static_ws_once[kMaxDevices];
+
+void* static_workspace_address(int dev) {
+    std::call_once(g_static_ws_once[dev], [dev] {
+        void* addr = nullptr;
+        g_static_ws_err[dev] = cudaGetSymbolAddress(&addr, g_static_split_ws);
+        g_static_ws_addr[dev] = g_static_ws_err[dev] == cudaSuccess ? addr : nullptr;
+    });
+    return g_static_ws_addr[dev];
+}
+
 }  // namespace
 
 // ---- C++ API ------------------------------------------------------------------------------------------
@@ -423,6 +446,41 @@ void mxfp6_gemm_force_tile(int ot, int M, int N, int Kp, int MT, int NT, int spl
     }
     run(ot, Route{MT, NT, splits}, M, N, Kp, dA, dBsh, dsA, dsB, dD, A_row_bytes, B_row_bytes, ws,
         static_cast<cudaStream_t>(stream));
+}
+
+void mxfp6_gemm_static_workspace(int ot, int M, int N, int Kp, const void* dA, const void* dBsh,
+                                 const uint8_t* dsA, const uint8_t* dsB, void* dD, int A_row_bytes,
+                                 int B_row_bytes, void* stream) {
+    t_last_error = MXFP6_OK;
+    if (!validate(ot, M, N, Kp, dA, dBsh, dsA, dsB, dD, A_row_bytes, B_row_bytes)) return;
+    const Route r = route_for(M, N, Kp, sm_count());
+    void* ws = nullptr;
+    if (r.splits > 1) {
+        const size_t need = splitk_bytes(M, N, r.splits);
+        if (need > kStaticWorkspaceBytes) {
+            set_error(MXFP6_ERR_WORKSPACE,
+                      "%dx%dx%d splits K %d ways and needs %zu bytes of split-K scratch; the library's "
+                      "static workspace holds %zu bytes. Use mxfp6_gemm with a caller workspace.",
+                      M, N, Kp, r.splits, need, kStaticWorkspaceBytes);
+            return;
+        }
+        const int dev = current_device();
+        if (dev < 0 || dev >= kMaxDevices) {
+            set_error(MXFP6_ERR_CUDA, "no CUDA device");
+            return;
+        }
+        ws = static_workspace_address(dev);
+        if (!ws) {
+            set_error(MXFP6_ERR_CUDA, "cudaGetSymbolAddress for the static split-K workspace failed: %s",
+                      cudaGetErrorString(g_static_ws_err[dev]));
+            return;
+        }
+    }
+    run(ot, r, M, N, Kp, dA, dBsh, dsA, dsB, dD, A_row_bytes, B_row_bytes, ws, static_cast<cudaStream_t>(stream));
+}
+
+size_t mxfp6_static_workspace_bytes(void) {
+    return kStaticWorkspaceBytes;
 }
 
 int mxfp6_last_error(void) {

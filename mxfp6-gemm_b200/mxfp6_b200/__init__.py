@@ -48,6 +48,10 @@ _force = _fn("mxfp6_gemm_force_tile", None,
              [C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p,
               C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_size_t,
               C.c_void_p])
+_static_ws_gemm = _fn("mxfp6_gemm_static_workspace", None,
+                      [C.c_int, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
+                       C.c_void_p, C.c_int, C.c_int, C.c_void_p])
+static_workspace_bytes = _fn("mxfp6_static_workspace_bytes", C.c_size_t, [])
 _ws = _fn("mxfp6_gemm_workspace_size", C.c_size_t, [C.c_int, C.c_int, C.c_int])
 _choose = _fn("mxfp6_choose_tile", None, [C.c_int, C.c_int, C.c_int, C.POINTER(C.c_int)])
 _k_tile = _fn("mxfp6_k_tile", C.c_int, [])
@@ -125,6 +129,14 @@ def gemm_force_tile(ot, M, N, Kp, MT, NT, splits, dA, dBsh, dsA, dsB, dD, A_row_
     s = 0 if stream is None else (stream.cuda_stream if hasattr(stream, "cuda_stream") else _addr(stream))
     _force(int(ot), M, N, Kp, MT, NT, splits, _addr(dA), _addr(dBsh), _addr(dsA), _addr(dsB), _addr(dD),
            A_row_bytes, B_row_bytes, _addr(ws), ws_bytes, s)
+
+
+def gemm_static_workspace(ot, M, N, Kp, dA, dBsh, dsA, dsB, dD, A_row_bytes, B_row_bytes, stream=None):
+    """mxfp6_gemm_static_workspace: gemm() without a caller workspace, for callers that cannot
+    allocate device memory (split-K partials go to the library's fixed 32 MiB array)."""
+    s = 0 if stream is None else (stream.cuda_stream if hasattr(stream, "cuda_stream") else _addr(stream))
+    _static_ws_gemm(int(ot), M, N, Kp, _addr(dA), _addr(dBsh), _addr(dsA), _addr(dsB), _addr(dD), A_row_bytes,
+                    B_row_bytes, s)
 
 
 def last_error_string() -> str:
