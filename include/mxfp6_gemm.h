@@ -64,8 +64,14 @@ void mxfp6_gemm_stream(int ot, int M, int N, int Kp, const void* dA, const void*
                        const uint8_t* dsA, const uint8_t* dsB, void* dD, int A_row_bytes,
                        int B_row_bytes, void* ws, size_t ws_bytes, void* stream);
 
-/* Split-K workspace bytes gemm() wants for (M,N,Kp); 0 when the route does not split. */
+/* Split-K workspace bytes gemm() wants for (M,N,Kp); 0 when the route does not split. The
+ * query has no output type, so this is the largest need over the output types: FP32 output
+ * splits long K into more segments to hold its tolerance. */
 size_t mxfp6_gemm_workspace_size(int M, int N, int Kp);
+
+/* The same for one output type (no counterpart in the reference): a caller that knows ot can
+ * allocate exactly what that call uses. */
+size_t mxfp6_gemm_workspace_size_out(int ot, int M, int N, int Kp);
 
 /* Route for (M,N,Kp): writes MT, NT, MPW, NPW into out[0..3]. */
 void mxfp6_choose_tile(int M, int N, int Kp, int* out4);

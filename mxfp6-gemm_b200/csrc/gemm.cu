@@ -322,12 +322,17 @@ bool run(int ot, const Route& r, int M, int N, int Kp, const void* dA, const voi
     }
 }
 
+// Route for an output type: FP32 output keeps split segments short enough for its tolerance.
+Route route_for_out(int ot, int M, int N, int Kp) {
+    return route_for(M, N, Kp, sm_count(), ot == MXFP6_OUT_F32 ? fp32_min_splits(Kp) : 1);
+}
+
 void gemm_entry(int ot, int M, int N, int Kp, const void* dA, const void* dB, const uint8_t* sA,
                 const uint8_t* sB, void* dD, int Ar, int Br, void* ws, size_t ws_bytes,
                 cudaStream_t stream) {
     t_last_error = MXFP6_OK;
     if (!validate(ot, M, N, Kp, dA, dB, sA, sB, dD, Ar, Br)) return;
-    Route r = route_for(M, N, Kp, sm_count());
+    Route r = route_for_out(ot, M, N, Kp);
     if (r.splits > 1) {
         const size_t need = splitk_bytes(M, N, r.splits);
         if (!ws || ws_bytes < need || !aligned(ws, 16)) {
@@ -374,9 +379,15 @@ TileChoice choose_tile(int M, int N, int Kp) {
     return TileChoice{r.MT, r.NT, r.MT / 32, r.NT / 32};
 }
 
+// The query has no output type (same signature as the reference), so it returns the larger of
+// the FP16/BF16 and FP32 needs: a workspace sized here fits every call on this shape.
 size_t gemm_workspace_size(int M, int N, int Kp) {
-    Route r = route_for(M, N, Kp, sm_count());
-    return r.splits > 1 ? splitk_bytes(M, N, r.splits) : 0;
+    size_t need = 0;
+    for (int ot : {MXFP6_OUT_F16, MXFP6_OUT_F32}) {
+        const Route r = route_for_out(ot, M, N, Kp);
+        if (r.splits > 1 && splitk_bytes(M, N, r.splits) > need) need = splitk_bytes(M, N, r.splits);
+    }
+    return need;
 }
 
 void gemm(OutType ot, int M, int N, int Kp, const void* dA, const void* dBsh, const uint8_t* dsA,
@@ -407,6 +418,12 @@ void mxfp6_gemm_stream(int ot, int M, int N, int Kp, const void* dA, const void*
 
 size_t mxfp6_gemm_workspace_size(int M, int N, int Kp) {
     return gemm_workspace_size(M, N, Kp);
+}
+
+size_t mxfp6_gemm_workspace_size_out(int ot, int M, int N, int Kp) {
+    if (ot < MXFP6_OUT_F32 || ot > MXFP6_OUT_BF16) return 0;
+    const Route r = route_for_out(ot, M, N, Kp);
+    return r.splits > 1 ? splitk_bytes(M, N, r.splits) : 0;
 }
 
 void mxfp6_choose_tile(int M, int N, int Kp, int* out4) {
@@ -453,7 +470,7 @@ void mxfp6_gemm_static_workspace(int ot, int M, int N, int Kp, const void* dA, c
                                  int B_row_bytes, void* stream) {
     t_last_error = MXFP6_OK;
     if (!validate(ot, M, N, Kp, dA, dBsh, dsA, dsB, dD, A_row_bytes, B_row_bytes)) return;
-    const Route r = route_for(M, N, Kp, sm_count());
+    const Route r = route_for_out(ot, M, N, Kp);
     void* ws = nullptr;
     if (r.splits > 1) {
         const size_t need = splitk_bytes(M, N, r.splits);

@@ -53,6 +53,7 @@ _static_ws_gemm = _fn("mxfp6_gemm_static_workspace", None,
                        C.c_void_p, C.c_int, C.c_int, C.c_void_p])
 static_workspace_bytes = _fn("mxfp6_static_workspace_bytes", C.c_size_t, [])
 _ws = _fn("mxfp6_gemm_workspace_size", C.c_size_t, [C.c_int, C.c_int, C.c_int])
+_ws_out = _fn("mxfp6_gemm_workspace_size_out", C.c_size_t, [C.c_int, C.c_int, C.c_int, C.c_int])
 _choose = _fn("mxfp6_choose_tile", None, [C.c_int, C.c_int, C.c_int, C.POINTER(C.c_int)])
 _k_tile = _fn("mxfp6_k_tile", C.c_int, [])
 _kpad = _fn("mxfp6_kpad", C.c_int, [C.c_int])
@@ -100,8 +101,9 @@ def choose_tile(M: int, N: int, Kp: int) -> TileChoice:
     return TileChoice(*out)
 
 
-def gemm_workspace_size(M: int, N: int, Kp: int) -> int:
-    return _ws(M, N, Kp)
+def gemm_workspace_size(M: int, N: int, Kp: int, ot=None) -> int:
+    """Split-K workspace bytes: for every output type (as the reference's query), or for `ot`."""
+    return _ws(M, N, Kp) if ot is None else _ws_out(int(ot), M, N, Kp)
 
 
 def _addr(x) -> int:

@@ -188,6 +188,17 @@ def test_baseline_configs_sampled(lib, oracle, cfg):
     check(D, _ref(oracle, ops, rows), ot, oracle, rows=rows, label=cfg)
 
 
+@pytest.mark.parametrize("M,N,K", [(2048, 1024, 105728), (1024, 512, 105728), (256, 384, 32768)])
+def test_long_k_fp32_within_tolerance(lib, oracle, M, N, K):
+    """FP32 output at long K: the route keeps split segments short enough (FP32_SEGMENT_K) that
+    the result stays within 1e-5 (norm-wise) of the sequential FP32 oracle."""
+    from gpu_helpers import check, run_gemm, sample_rows
+    ops, dev = _setup(M, N, K, kind="codes", seed=5, exp_range=(109, 127))
+    rows = sample_rows(M, 16)
+    D = run_gemm(dev, lib.OutType.F32)
+    check(D, _ref(oracle, ops, rows), lib.OutType.F32, oracle, rows=rows, label=f"{M}x{N}x{K} fp32")
+
+
 def test_small_workspace_falls_back_unsplit(lib, oracle, capfd):
     """A shape that wants split-K but gets too small a workspace runs unsplit, warns, and is right."""
     from gpu_helpers import check, run_gemm, sample_rows

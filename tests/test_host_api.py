@@ -129,6 +129,15 @@ def test_route_examples(lib):
     assert lib.choose_tile(8192, 8192, 8192).MT == 256  # CTA-pair tile on machine-filling shapes
 
 
+def test_workspace_query_per_output_type(lib):
+    """The type-free query covers every output type; FP32 splits long K into short segments."""
+    for M, N, K in [(2048, 1024, 105728), (256, 384, 32768), (8192, 8192, 8192), (1024, 512, 105728)]:
+        per = [lib.gemm_workspace_size(M, N, K, ot) for ot in lib.OutType]
+        assert lib.gemm_workspace_size(M, N, K) == max(per)
+    assert lib.gemm_workspace_size(2048, 1024, 105728, lib.OutType.F32) == 9 * 2048 * 1024 * 4
+    assert lib.gemm_workspace_size(2048, 1024, 105728, lib.OutType.F16) < 9 * 2048 * 1024 * 4
+
+
 def test_workspace_query_on_degenerate_shapes(lib):
     """Sub-tile shapes must not crash the query (reference: tests/test_gemm.cpp:362-365)."""
     for M, N, K in [(192, 256, 32832), (256, 192, 3072), (64, 64, 3072), (0, 128, 128), (128, 128, 0)]:

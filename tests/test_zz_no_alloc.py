@@ -13,11 +13,13 @@ import numpy as np
 import pytest
 import torch
 
-# A shape whose route splits K (2 ways here) and whose partials fit in the 32 MiB array.
-M, N, K = 2048, 1024, 105728
+# Shapes whose route splits K and whose partials fit in the 32 MiB array: FP16 output splits
+# 2048x1024x105728 two ways; FP32 output keeps split segments short (9 ways at this K), so it
+# uses a smaller M x N.
+SHAPES = {"F16": (2048, 1024, 105728), "F32": (1024, 512, 105728)}
 
 
-def _operands():
+def _operands(M, N, K):
     from gpu_helpers import DeviceOperands
     from mxfp6_b200.synth import make_operands
     ops = make_operands(M, N, K, kind="codes", seed=77, exp_range=(109, 127))
@@ -48,8 +50,9 @@ def test_static_workspace_matches_caller_workspace(lib, ot):
     if not torch.cuda.is_available():
         pytest.skip("no CUDA device")
     from gpu_helpers import FP32_TOL, run_gemm
-    assert 0 < lib.gemm_workspace_size(M, N, K) <= lib.static_workspace_bytes()
-    ops, dev = _operands()
+    M, N, K = SHAPES[ot]
+    assert 0 < lib.gemm_workspace_size(M, N, K, lib.OutType[ot]) <= lib.static_workspace_bytes()
+    ops, dev = _operands(M, N, K)
     o = lib.OutType[ot]
     expected = run_gemm(dev, o)  # existing entry point, caller workspace from gemm_workspace_size()
     tdt = torch.float32 if o == lib.OutType.F32 else torch.float16
