@@ -52,6 +52,9 @@ CONFIG_DESC = {
 }
 METRIC = "MXFP6 GEMM TFLOPS (2*M*N*K / device time)"
 L2_FLUSH_BYTES = 256 << 20
+# DRAM bytes (read + write) per launch of the dominant kernel, from one ncu capture of this
+# bench's own command (profiles/gemm_mxfp6_sm100_pair_cfg2.md); None where not captured yet.
+NCU_TRAFFIC_BYTES = {"cfg2": 256_694_272 + 117_018_112}
 
 
 def load_peaks():
@@ -163,12 +166,20 @@ def cpu_reference_sample(cfg_name, target_s=10.0, threads=None, rows_override=No
             return o.gemm(ops.A[:rows], ops.sA[:rows], ops.Bt, ops.sB, ops.Kp, threads=threads)
 
     if rows_override is None:
-        probe = min(ops.M, threads)
+        # A warm-up call, then two timed sizes separate the per-call cost (each call dequantises
+        # all of B per thread) from the per-row cost, so the sample lands near target_s.
+        run(min(ops.M, threads))
+        r1, r2 = min(ops.M, 4 * threads), min(ops.M, 16 * threads)
         t0 = time.perf_counter()
-        run(probe)
-        t_probe = time.perf_counter() - t0
-        rows = int(probe * target_s / max(t_probe, 1e-3))
-        rows = max(probe, min(ops.M, rows // threads * threads if rows >= threads else rows))
+        run(r1)
+        t1 = time.perf_counter() - t0
+        t0 = time.perf_counter()
+        run(r2)
+        t2 = time.perf_counter() - t0
+        per_row = (t2 - t1) / (r2 - r1) if r2 > r1 and t2 > t1 else t2 / max(r2, 1)
+        fixed = max(0.0, t2 - per_row * r2)
+        rows = int((target_s - fixed) / max(per_row, 1e-9))
+        rows = max(r2, min(ops.M, rows // threads * threads if rows >= threads else rows))
     else:
         rows = min(rows_override, ops.M)
     t0 = time.perf_counter()
@@ -348,6 +359,8 @@ def run_ours(args):
         cpu = {"value": v, "unit": "TFLOPS", "cores": cores, "kind": kind_s, "sample": sample}
 
     bf16_peak, hbm_peak, basis = load_peaks()
+    out_bytes = {lib.OutType.F32: 4, lib.OutType.F16: 2, lib.OutType.BF16: 2}[ot]
+    algo_bytes = (M + N) * Kp * 3 // 4 + (M + N) * (Kp // 32) + M * N * out_bytes
     peak = 2.0 * bf16_peak
     kernel_ms = min(per)  # dominant kernel: the GEMM (plus the split-K reduce when routed)
     achieved = flops_rank / (ms * 1e-3) / 1e12
@@ -365,7 +378,8 @@ def run_ours(args):
                        "parallelism": f"N-sharded x{world}, no collective on the GEMM path",
                        "l2": "256 MiB buffer written before every timed step (L2 flushed)"},
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                         "frac": achieved / peak, "traffic": None,
+                         "frac": achieved / peak, "traffic": NCU_TRAFFIC_BYTES.get(args.config) if world == 1 else None,
+                         "algorithmic_bytes": algo_bytes,
                          "peak_basis": f"2 x {basis} cuBLAS bf16 dense ({bf16_peak:.1f} TFLOP/s): B200's dense "
                                        f"FP8/FP6 tensor rate is twice bf16",
                          "best_step_ms": kernel_ms},
