@@ -104,13 +104,13 @@ bool make_fp6_tmap(CUtensorMap* map, const void* ptr, int rows, int Kp, int row_
 
 // Tiled scales viewed as [row_atoms][k_slabs][128 x u32] (512-byte atoms), read one or two
 // atoms at a time; atoms past the last row block read as zero.
-bool make_sf_tmap(CUtensorMap* map, const void* ptr, int rows, int Kp, int box_atoms) {
+bool make_sf_tmap(CUtensorMap* map, const void* ptr, int rows, int Kp, int box_atoms, int box_slabs = 1) {
     EncodeTiledFn fn = encode_fn();
     if (!fn) return false;
     const int k_slabs = Kp / 128, atoms = (rows + 127) / 128;
     cuuint64_t dims[3] = {128u, (cuuint64_t)k_slabs, (cuuint64_t)atoms};
     cuuint64_t strides[2] = {512u, (cuuint64_t)k_slabs * 512u};
-    cuuint32_t box[3] = {128u, 1u, (cuuint32_t)box_atoms};
+    cuuint32_t box[3] = {128u, (cuuint32_t)box_slabs, (cuuint32_t)box_atoms};
     cuuint32_t estr[3] = {1u, 1u, 1u};
     CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT32, 3, const_cast<void*>(ptr), dims, strides, box, estr,
                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -232,7 +232,7 @@ bool launch_pair(int M, int N, int Kp, const void* dA, const void* dB, const uin
     }
     CUtensorMap tmA, tmB, tmSA, tmSB;
     if (!make_fp6_tmap(&tmA, dA, M, Kp, A_row_bytes, 128) || !make_fp6_tmap(&tmB, dB, N, Kp, B_row_bytes, 128) ||
-        !make_sf_tmap(&tmSA, sA, M, Kp, 1) || !make_sf_tmap(&tmSB, sB, N, Kp, 2)) {
+        !make_sf_tmap(&tmSA, sA, M, Kp, 1, C::SUB) || !make_sf_tmap(&tmSB, sB, N, Kp, 2, C::SUB)) {
         set_error(MXFP6_ERR_CUDA, "cuTensorMapEncodeTiled failed for %dx%dx%d", M, N, Kp);
         return false;
     }

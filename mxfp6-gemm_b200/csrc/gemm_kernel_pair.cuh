@@ -20,23 +20,34 @@
 // Every wait is bounded (see gemm_kernel.cuh); a timeout also raises the peer's abort flag.
 #include "gemm_kernel.cuh"
 
+// 128-deep K slabs per pipeline stage (1 or 2).
+#ifndef MXFP6_PAIR_SUB
+#define MXFP6_PAIR_SUB 1
+#endif
+
 namespace mxfp6 {
 namespace kern {
 
 struct PairConfig {
     static constexpr int BM = 256;  // rows per pair tile (128 per CTA)
     static constexpr int BN = 256;  // columns per pair tile (B rows 128 per CTA)
-    static constexpr int STAGES = 6;
-    static constexpr int A_BYTES = 128 * BK;
-    static constexpr int B_BYTES = 128 * BK;
+    static constexpr int SUB = MXFP6_PAIR_SUB;           // 128-deep slabs per stage
+    static constexpr int STAGES = SUB == 1 ? 6 : 3;
+    static constexpr int SLAB_BYTES = 128 * BK;          // one 128-row x 128-K box in shared memory
+    static constexpr int A_BYTES = SUB * SLAB_BYTES;
+    static constexpr int B_BYTES = SUB * SLAB_BYTES;
     static constexpr int AB_STAGE = A_BYTES + B_BYTES;
-    static constexpr int SF_STAGE = 512 + 1024;  // own A atom, both B atoms
-    static constexpr uint32_t TX_PER_CTA = 2 * (128 * BK * 3 / 4) + 512 + 1024;
-    static constexpr uint32_t TX_STAGE = 2 * TX_PER_CTA;  // leader's barrier counts both CTAs
+    static constexpr int SFA_BYTES = SUB * 512;          // own A atom per slab
+    static constexpr int SF_STAGE = SFA_BYTES + SUB * 1024;  // then both B atoms per slab
+    static constexpr uint32_t SLAB_TX = 2 * (128 * BK * 3 / 4);  // packed A + B bytes per CTA
+    static constexpr uint32_t tx_stage(int nsub) {                // leader's barrier counts both CTAs
+        return 2 * (nsub * SLAB_TX + SF_STAGE);
+    }
     static constexpr int TMEM_COLS = 512;
     static constexpr int BUF1_COL = 224;  // buffer 1 starts 32 columns below buffer 0's end
-    static constexpr int TMEM_SFA = 480;
-    static constexpr int TMEM_SFB = 484;
+    static constexpr int TMEM_SF = 480;  // per slab of a stage: A scales (4 columns), B scales (8)
+    static constexpr int SF_SET_COLS = 12;
+    static_assert(TMEM_SF + SUB * SF_SET_COLS <= 512, "tensor memory budget");
     static constexpr int EPI_WARPS = 4;
     static constexpr int BAR_BYTES = 256;
     static constexpr int SMEM_BYTES = 1024 + STAGES * (AB_STAGE + SF_STAGE) + BAR_BYTES;
@@ -137,21 +148,26 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 const TileCoord tc = decode_tile(t, p);
                 const int a_row = tc.mb * C::BM + 128 * (int)rank;
                 const int b_row = tc.nb * C::BN + 128 * (int)rank;
-                for (int i = 0; i < tc.kb_count; i++) {
+                for (int i = 0; i < tc.kb_count; i += C::SUB) {
                     if (!sm100::wait_parity_bounded(empty_bar(stage), phase ^ 1u, abort_flag, WAIT_BUDGET)) {
                         if (!*abort_flag) raise(0x1u);
                         ok = false;
                         break;
                     }
                     const int kb = tc.kb_begin + i;
+                    const int nsub = tc.kb_count - i < C::SUB ? tc.kb_count - i : C::SUB;
                     const uint32_t fb = sm100::mapa_shared(full_bar(stage), 0);
-                    if (rank == 0) sm100::mbar_arrive_expect_tx(full_bar(stage), C::TX_STAGE);
+                    if (rank == 0) sm100::mbar_arrive_expect_tx(full_bar(stage), C::tx_stage(nsub));
                     const uint32_t a_dst = ab_base + stage * C::AB_STAGE;
-                    sm100::tma_load_2d_pair(a_dst, &tmA, fb, kb * BK, a_row);
-                    sm100::tma_load_2d_pair(a_dst + C::A_BYTES, &tmB, fb, kb * BK, b_row);
+                    for (int j = 0; j < nsub; j++) {
+                        sm100::tma_load_2d_pair(a_dst + j * C::SLAB_BYTES, &tmA, fb, (kb + j) * BK, a_row);
+                        sm100::tma_load_2d_pair(a_dst + C::A_BYTES + j * C::SLAB_BYTES, &tmB, fb, (kb + j) * BK,
+                                                b_row);
+                    }
+                    // scale boxes are SUB slabs deep; a slab past the end reads as zero
                     const uint32_t sf_dst = sf_base + stage * C::SF_STAGE;
                     sm100::tma_load_3d_pair(sf_dst, &tmSA, fb, 0, kb, tc.mb * 2 + (int)rank);
-                    sm100::tma_load_3d_pair(sf_dst + 512, &tmSB, fb, 0, kb, tc.nb * 2);
+                    sm100::tma_load_3d_pair(sf_dst + C::SFA_BYTES, &tmSB, fb, 0, kb, tc.nb * 2);
                     issued_mask |= 1u << stage;
                     issued_phase = (issued_phase & ~(1u << stage)) | (phase << stage);
                     if (++stage == C::STAGES) {
@@ -182,8 +198,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             for (int k = 0; k < BK / 32; k++) idesc_k[k] = sm100::idesc_with_sf_ids(idesc, k, k);
             const uint64_t a_desc0 = sm100::make_kmajor_sw128_desc(ab_base);
             const uint64_t b_desc0 = sm100::make_kmajor_sw128_desc(ab_base + C::A_BYTES);
-            const uint32_t sfa_t = tmem_base + C::TMEM_SFA;
-            const uint32_t sfb_t = tmem_base + C::TMEM_SFB;
             int stage = 0;
             uint32_t phase = 0;
             bool ok = true, issued = false;
@@ -205,22 +219,32 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 // slab's barrier without blocking right after issuing the current one, and
                 // blocks only when that slab's data has not landed yet.
                 bool ready = sm100::mbar_test_wait(full_bar(stage), phase);
-                for (int i = 0; i < tc.kb_count; i++) {
+                for (int i = 0; i < tc.kb_count; i += C::SUB) {
                     if (!ready && !sm100::wait_parity_bounded(full_bar(stage), phase, abort_flag, WAIT_BUDGET)) {
                         if (!*abort_flag) raise(0x2u);
                         ok = false;
                         break;
                     }
+                    const int nsub = tc.kb_count - i < C::SUB ? tc.kb_count - i : C::SUB;
                     const uint32_t sf_src = sf_base + stage * C::SF_STAGE;
-                    sm100::tc_cp_32x128b_warpx4_pair(sfa_t, sm100::make_sf_desc(sf_src));
-                    sm100::tc_cp_32x128b_warpx4_pair(sfb_t, sm100::make_sf_desc(sf_src + 512));
-                    sm100::tc_cp_32x128b_warpx4_pair(sfb_t + 4, sm100::make_sf_desc(sf_src + 1024));
-                    const uint32_t off16 = (uint32_t)(stage * C::AB_STAGE) >> 4;  // descriptor address units
+                    for (int j = 0; j < nsub; j++) {  // scale atoms of slab j -> scale set j
+                        const uint32_t sfa_t = tmem_base + C::TMEM_SF + C::SF_SET_COLS * j;
+                        sm100::tc_cp_32x128b_warpx4_pair(sfa_t, sm100::make_sf_desc(sf_src + 512 * j));
+                        sm100::tc_cp_32x128b_warpx4_pair(sfa_t + 4, sm100::make_sf_desc(sf_src + C::SFA_BYTES + 512 * j));
+                        sm100::tc_cp_32x128b_warpx4_pair(sfa_t + 8, sm100::make_sf_desc(sf_src + C::SFA_BYTES +
+                                                                                        512 * (C::SUB + j)));
+                    }
+                    for (int j = 0; j < nsub; j++) {
+                        const uint32_t sfa_t = tmem_base + C::TMEM_SF + C::SF_SET_COLS * j;
+                        const uint32_t sfb_t = sfa_t + 4;
+                        const uint32_t off16 = (uint32_t)(stage * C::AB_STAGE + j * C::SLAB_BYTES) >> 4;
 #pragma unroll
-                    for (int k = 0; k < BK / 32; k++) {
-                        const uint32_t sel = (uint32_t)k << 30;
-                        sm100::tc_mma_mxf8f6f4_pair(d_taddr, a_desc0 + off16 + 2 * k, b_desc0 + off16 + 2 * k,
-                                                    idesc_k[k], sfa_t | sel, sfb_t | sel, (i > 0 || k > 0) ? 1u : 0u);
+                        for (int k = 0; k < BK / 32; k++) {
+                            const uint32_t sel = (uint32_t)k << 30;
+                            sm100::tc_mma_mxf8f6f4_pair(d_taddr, a_desc0 + off16 + 2 * k, b_desc0 + off16 + 2 * k,
+                                                        idesc_k[k], sfa_t | sel, sfb_t | sel,
+                                                        (i > 0 || j > 0 || k > 0) ? 1u : 0u);
+                        }
                     }
                     issued = true;
                     sm100::tc_commit_pair(empty_bar(stage), 0x3);
@@ -250,10 +274,17 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         for (int t = cluster_id; t < total_tiles; t += num_clusters, local++) {
             const TileCoord tc = decode_tile(t, p);
             const int b = local & 1;
-            if (!sm100::wait_parity_bounded(acc_full0 + 8u * b, (local >> 1) & 1, abort_flag, WAIT_BUDGET)) {
-                if (!*abort_flag) raise(0x4u);
+            // One lane per warp polls the barrier (fewer pollers on shared memory while the main
+            // loop runs); the warp then confirms the completed phase without blocking.
+            int got = 1;
+            if (lane == 0)
+                got = sm100::wait_parity_bounded(acc_full0 + 8u * b, (local >> 1) & 1, abort_flag, WAIT_BUDGET) ? 1 : 0;
+            got = __shfl_sync(0xffffffffu, got, 0);
+            if (!got) {
+                if (lane == 0 && !*abort_flag) raise(0x4u);
                 break;
             }
+            sm100::mbar_try_wait(acc_full0 + 8u * b, (local >> 1) & 1);
             sm100::tc_fence_after();
             const int row = tc.mb * C::BM + 128 * (int)rank + 32 * quarter + lane;
             const int col0 = tc.nb * C::BN;
