@@ -135,6 +135,15 @@ int mxfp6_probe_tma_fp6(const void* dsrc, int rows, int Kp, int row_bytes, int s
 void mxfp6_quantize(const float* mat, int rows, int cols, uint8_t* packed, uint8_t* scales,
                     int nthreads);
 
+/* quantize_to_mxfp6 on the GPU (reference: include/mxfp6/preprocess.hpp:51-97), bit-identical to
+ * the host version: device float [rows][cols] (cols % 32 == 0, 16-byte aligned) -> device packed
+ * FP6 [rows][3*cols/4] (4-byte aligned) and scales, raw [rows][cols/32] (scale_layout 0) or
+ * directly in the GEMM's tiled atom layout (scale_layout 1, cols % 128 == 0; rows past the
+ * last full atom are not written). rows <= 65535. Asynchronous on `stream` (NULL = legacy).
+ * Returns an mxfp6_status. */
+int mxfp6_quantize_device(const float* d_mat, int rows, int cols, uint8_t* d_packed, uint8_t* d_scales,
+                          int scale_layout, void* stream);
+
 /* dequantize_mxfp6 (reference: include/mxfp6/preprocess.hpp:100-109). */
 void mxfp6_dequantize(const uint8_t* packed, const uint8_t* scales, int rows, int cols,
                       float* out);

@@ -372,6 +372,10 @@ void* static_workspace_address(int dev) {
 
 }  // namespace
 
+void note_launch() {
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+}
+
 // ---- C++ API ------------------------------------------------------------------------------------------
 
 TileChoice choose_tile(int M, int N, int Kp) {

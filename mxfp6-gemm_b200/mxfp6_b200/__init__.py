@@ -62,6 +62,8 @@ _last_error_string = _fn("mxfp6_last_error_string", C.c_char_p, [])
 _device_status = _fn("mxfp6_device_status", C.c_int, [])
 launch_count = _fn("mxfp6_launch_count", C.c_uint64, [])
 _quantize = _fn("mxfp6_quantize", None, [_f32p, C.c_int, C.c_int, _u8p, _u8p, C.c_int])
+_quantize_dev = _fn("mxfp6_quantize_device", C.c_int,
+                    [C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_int, C.c_void_p])
 _dequantize = _fn("mxfp6_dequantize", None, [_u8p, _u8p, C.c_int, C.c_int, _f32p])
 _tiled_bytes = _fn("mxfp6_tiled_scale_bytes", C.c_size_t, [C.c_int, C.c_int])
 _tile = _fn("mxfp6_tile_scales", None, [_u8p, C.c_int, C.c_int, _u8p])
@@ -181,6 +183,12 @@ def quantize_to_mxfp6(mat: np.ndarray, threads: int = 0) -> QuantizedMatrix:
     scales = np.empty((rows, cols // 32), np.uint8)
     _quantize(mat, rows, cols, packed, scales, threads)
     return QuantizedMatrix(packed, scales, rows, cols)
+
+
+def quantize_device(d_mat, rows, cols, d_packed, d_scales, tiled=False, stream=None) -> int:
+    """quantize_to_mxfp6 on the GPU (device pointers); scales raw or in the GEMM's atom layout."""
+    s = 0 if stream is None else (stream.cuda_stream if hasattr(stream, "cuda_stream") else _addr(stream))
+    return _quantize_dev(_addr(d_mat), rows, cols, _addr(d_packed), _addr(d_scales), 1 if tiled else 0, s)
 
 
 def dequantize_mxfp6(q: QuantizedMatrix) -> np.ndarray:

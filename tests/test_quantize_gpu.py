@@ -1,0 +1,66 @@
+"""Device quantiser (mxfp6_quantize_device) against the host quantize_to_mxfp6, which the
+reference's golden vectors pin: packed codes and scales must match byte for byte, including
+NaN / Inf / zero / subnormal blocks, for both scale layouts."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _cuda():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+
+
+def _device_quantize(lib, mat, tiled):
+    rows, cols = mat.shape
+    d = torch.from_numpy(np.ascontiguousarray(mat, dtype=np.float32)).cuda()
+    packed = torch.full((rows, cols * 3 // 4), 0xA5, dtype=torch.uint8, device="cuda")
+    nsc = lib.tiled_scale_bytes(rows, cols) if tiled else rows * cols // 32
+    scales = torch.full((nsc,), 0xA5, dtype=torch.uint8, device="cuda")
+    assert lib.quantize_device(d, rows, cols, packed, scales, tiled) == lib.OK
+    torch.cuda.synchronize()
+    return packed.cpu().numpy(), scales.cpu().numpy()
+
+
+def _special_matrix(rows, cols, seed):
+    rng = np.random.default_rng(seed)
+    m = (rng.standard_normal((rows, cols)) * np.exp(rng.uniform(-30, 30, (rows, 1)))).astype(np.float32)
+    m[0] = 0.0
+    m[1, 3] = np.nan
+    m[2, :40] = np.inf
+    m[3, 7] = -np.inf
+    m[4] = np.float32(1e-41)                 # subnormal inputs
+    m[5, ::5] = np.float32(7.5)
+    m[6] *= np.float32(1e38)
+    m[7, :32] = np.float32(-0.0)
+    m[8, :32] = np.nan                       # an all-NaN block
+    return m
+
+
+def test_golden_quantisation(lib, golden):
+    p, s = _device_quantize(lib, golden["quant_in"], tiled=False)
+    assert np.array_equal(p, golden["quant_packed"])
+    assert np.array_equal(s.reshape(golden["quant_scales"].shape), golden["quant_scales"])
+
+
+@pytest.mark.parametrize("rows,cols", [(128, 128), (200, 96), (257, 4160), (4096, 8192)])
+def test_matches_host_raw_scales(lib, rows, cols):
+    m = _special_matrix(rows, cols, rows + cols)
+    host = lib.quantize_to_mxfp6(m)
+    p, s = _device_quantize(lib, m, tiled=False)
+    assert np.array_equal(p, host.packed_data)
+    assert np.array_equal(s.reshape(rows, cols // 32), host.scales)
+
+
+@pytest.mark.parametrize("rows,cols", [(128, 256), (384, 1024), (256, 8192)])
+def test_matches_host_tiled_scales(lib, rows, cols):
+    m = _special_matrix(rows, cols, 7 * rows + cols)
+    host = lib.quantize_to_mxfp6(m)
+    p, s = _device_quantize(lib, m, tiled=True)
+    assert np.array_equal(p, host.packed_data)
+    assert np.array_equal(s, lib.preprocess_scale(host.scales, rows, cols))
