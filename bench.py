@@ -327,6 +327,30 @@ def run_ours(args):
         e2e_ms = float(t.item())
     e2e_value = flops_rank * world / (e2e_ms * 1e-3) / 1e12
 
+    # ---- activation quantisation on the device (cfg5: the step before the FFN GEMM) ----
+    quant = None
+    if args.config == "cfg5" and rank == 0:
+        xf = torch.randn((M, K), device=dev, dtype=torch.float32)
+        qa = torch.empty((M, Kp * 3 // 4), dtype=torch.uint8, device=dev)
+        qs = torch.empty(lib.tiled_scale_bytes(M, Kp), dtype=torch.uint8, device=dev)
+        for _ in range(3):
+            assert lib.quantize_device(xf, M, K, qa, qs, True, stream=stream) == lib.OK
+        q0 = torch.cuda.Event(enable_timing=True)
+        q1 = torch.cuda.Event(enable_timing=True)
+        reps = 20
+        q0.record(stream)
+        for _ in range(reps):
+            lib.quantize_device(xf, M, K, qa, qs, True, stream=stream)
+        q1.record(stream)
+        torch.cuda.synchronize()
+        qms = q0.elapsed_time(q1) / reps
+        qbytes = M * K * 4 + M * K * 3 // 4 + M * K // 32
+        _, hbm_peak_q, hbm_basis = load_peaks()
+        quant = {"what": f"quantize A [{M}x{K}] fp32 -> MXFP6 + tiled scales on the device", "ms": qms,
+                 "gbs": qbytes / (qms * 1e-3) / 1e9, "frac_hbm": qbytes / (qms * 1e-3) / 1e9 / hbm_peak_q,
+                 "peak_basis": f"{hbm_basis} copy bandwidth {hbm_peak_q:.0f} GB/s"}
+        del xf, qa, qs
+
     # ---- optional NCCL all-gather of the D shards (timed separately) ----
     allgather = None
     if world > 1 and not args.no_allgather:
@@ -392,6 +416,8 @@ def run_ours(args):
         }
         if allgather:
             line["allgather"] = allgather
+        if quant:
+            line["quantize_device"] = quant
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()

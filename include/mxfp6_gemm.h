@@ -160,6 +160,25 @@ void mxfp6_tile_scales(const uint8_t* scales, int rows, int cols, uint8_t* tiled
 /* Inverse of mxfp6_tile_scales (for checks). */
 void mxfp6_untile_scales(const uint8_t* tiled, int rows, int cols, uint8_t* scales);
 
+/* ---- import of buffers prepared for the reference library (gfx950 layouts) -------------------
+ * One-time host conversions, so weights preprocessed for the reference need no re-quantising. */
+
+/* Inverse of the reference's preshuffle_B (include/mxfp6/preprocess.hpp:182-207): ref_bsh holds
+ * (N/32)*(Kp_ref/64) tiles of 1536 bytes; out receives B^T packed rows [N][out_row_bytes], the
+ * first 3*Kp_ref/4 bytes of each row filled and the rest zeroed (pad Kp up to a multiple of 128
+ * and use out_row_bytes = 3*kpad(Kp_ref)/4). Returns an mxfp6_status. */
+int mxfp6_import_ref_B(const uint8_t* ref_bsh, int N, int Kp_ref, uint8_t* out, int out_row_bytes);
+
+/* Inverse of the reference's tile_scale(preprocess_scale(raw, dim, Kp_ref), group, subs)
+ * (include/mxfp6/preprocess.hpp:136-162,216-233): writes raw scales [dim][Kp_ref/32]. group is
+ * the reference's MPW/NPW for the route it tiled for, subs its K_TILE/64 (3). */
+int mxfp6_import_ref_scales(const uint8_t* ref_tiled, int dim, int Kp_ref, int group, int subs, uint8_t* raw_out);
+
+/* Copy rows of src_bytes_used bytes from a src_row_bytes stride to a dst_row_bytes stride,
+ * zero-filling each row's tail (re-padding A rows from the reference's Kp to this library's). */
+int mxfp6_repad_rows(const uint8_t* src, int rows, int src_row_bytes, int src_bytes_used, uint8_t* dst,
+                     int dst_row_bytes);
+
 #ifdef __cplusplus
 }
 #endif

@@ -68,6 +68,9 @@ _dequantize = _fn("mxfp6_dequantize", None, [_u8p, _u8p, C.c_int, C.c_int, _f32p
 _tiled_bytes = _fn("mxfp6_tiled_scale_bytes", C.c_size_t, [C.c_int, C.c_int])
 _tile = _fn("mxfp6_tile_scales", None, [_u8p, C.c_int, C.c_int, _u8p])
 _untile = _fn("mxfp6_untile_scales", None, [_u8p, C.c_int, C.c_int, _u8p])
+_imp_B = _fn("mxfp6_import_ref_B", C.c_int, [_u8p, C.c_int, C.c_int, _u8p, C.c_int])
+_imp_sc = _fn("mxfp6_import_ref_scales", C.c_int, [_u8p, C.c_int, C.c_int, C.c_int, C.c_int, _u8p])
+_repad = _fn("mxfp6_repad_rows", C.c_int, [_u8p, C.c_int, C.c_int, C.c_int, _u8p, C.c_int])
 _probe = _fn("mxfp6_probe_tma_fp6", C.c_int,
              [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_uint32, C.c_void_p])
 
@@ -227,6 +230,40 @@ def tile_scale(ps: np.ndarray, group: int = 0, subs: int = 0) -> np.ndarray:
 def untile_scales(tiled: np.ndarray, dim: int, K: int) -> np.ndarray:
     out = np.empty((dim, K // 32), np.uint8)
     _untile(np.ascontiguousarray(tiled, dtype=np.uint8), dim, K, out.reshape(-1))
+    return out
+
+
+# ---- import of buffers prepared for the reference library ------------------------------------------
+
+def import_ref_B(ref_bsh: np.ndarray, N: int, Kp_ref: int, Kp: int | None = None) -> np.ndarray:
+    """Reference preshuffle_B buffer -> B^T packed rows [N][3*Kp/4] (Kp = kpad(Kp_ref))."""
+    Kp = Kp or kpad(Kp_ref)
+    out = np.empty((N, Kp * 3 // 4), np.uint8)
+    rc = _imp_B(np.ascontiguousarray(ref_bsh, dtype=np.uint8), N, Kp_ref, out.reshape(-1), Kp * 3 // 4)
+    if rc != OK:
+        raise ValueError(f"mxfp6_import_ref_B failed ({rc})")
+    return out
+
+
+def import_ref_scales(ref_tiled: np.ndarray, dim: int, Kp_ref: int, group: int, subs: int = 3,
+                      Kp: int | None = None) -> np.ndarray:
+    """Reference tiled scales -> raw scales [dim][Kp/32]; blocks past Kp_ref get the finite 127."""
+    Kp = Kp or kpad(Kp_ref)
+    raw = np.empty((dim, Kp_ref // 32), np.uint8)
+    rc = _imp_sc(np.ascontiguousarray(ref_tiled, dtype=np.uint8), dim, Kp_ref, group, subs, raw.reshape(-1))
+    if rc != OK:
+        raise ValueError(f"mxfp6_import_ref_scales failed ({rc})")
+    out = np.full((dim, Kp // 32), 127, np.uint8)
+    out[:, :Kp_ref // 32] = raw
+    return out
+
+
+def repad_rows(src: np.ndarray, bytes_used: int, dst_row_bytes: int) -> np.ndarray:
+    src = np.ascontiguousarray(src, dtype=np.uint8)
+    out = np.empty((src.shape[0], dst_row_bytes), np.uint8)
+    rc = _repad(src.reshape(-1), src.shape[0], src.shape[1], bytes_used, out.reshape(-1), dst_row_bytes)
+    if rc != OK:
+        raise ValueError(f"mxfp6_repad_rows failed ({rc})")
     return out
 
 

@@ -124,6 +124,21 @@ class Reference:
         self._gemm_mt = _bind(lib, "ref_gemm_rows_mt", None,
                               [_u8p, _u8p, _u8p, _u8p, C.c_int, C.c_int, C.c_int, _f32p, C.c_int])
 
+    def preshuffle_B(self, Bt, sB, K):
+        Bt = np.ascontiguousarray(Bt)
+        N = Bt.shape[0]
+        out = np.empty(N // 32 * (K // 64) * 1536, np.uint8)
+        f = _bind(self.lib, "ref_preshuffle_B", None, [_u8p, _u8p, C.c_int, C.c_int, _u8p])
+        f(Bt, np.ascontiguousarray(sB), N, K, out)
+        return out
+
+    def tile_scales(self, raw, dim, K, group, subs):
+        q = _bind(self.lib, "ref_tiled_scale_bytes", C.c_size_t, [C.c_int, C.c_int, C.c_int, C.c_int])
+        out = np.empty(q(dim, K, group, subs), np.uint8)
+        f = _bind(self.lib, "ref_tile_scales", None, [_u8p, C.c_int, C.c_int, C.c_int, C.c_int, _u8p])
+        f(np.ascontiguousarray(raw, dtype=np.uint8).reshape(-1), dim, K, group, subs, out)
+        return out
+
     def pack(self, codes: np.ndarray) -> np.ndarray:
         codes = np.ascontiguousarray(codes, dtype=np.uint8).reshape(-1)
         out = np.empty(codes.size * 3 // 4, np.uint8)

@@ -11,6 +11,7 @@
 //   ref_e8m0_to_float / ref_float_to_e8m0 mxfp6::e8m0_to_float / float_to_e8m0
 //   ref_pack_fp6 / ref_unpack_fp6         mxfp6::pack_fp6 / unpack_fp6
 //   ref_quantize                          mxfp6::quantize_to_mxfp6
+//   ref_preshuffle_B / ref_tile_scales    mxfp6::preshuffle_B / tile_scale(preprocess_scale(..))
 //   ref_gemm                              mxfp6::mxfp6_gemm_ref (single thread, as shipped)
 //   ref_gemm_rows_mt                      mxfp6_gemm_ref on row slices of A over threads (each
 //                                         output element keeps its summation order)
@@ -48,6 +49,23 @@ void ref_quantize(const float* mat, int rows, int cols, uint8_t* packed, uint8_t
     QuantizedMatrix q = quantize_to_mxfp6(mat, rows, cols);
     std::memcpy(packed, q.packed_data.data(), q.packed_data.size());
     std::memcpy(scales, q.scales.data(), q.scales.size());
+}
+
+// preshuffle_B on B^T packed [N][3K/4] (N % 32 == 0, K % 64 == 0) -> (N/32)*(K/64)*1536 bytes.
+void ref_preshuffle_B(const uint8_t* Bt, const uint8_t* sB, int N, int K, uint8_t* out) {
+    QuantizedMatrix q = make_q(Bt, sB, N, K);
+    PreshuffledB pb = preshuffle_B(q);
+    std::memcpy(out, pb.data.data(), pb.data.size());
+}
+
+// tile_scale(preprocess_scale(raw, dim, K), group, subs) -> out (size returned by the query below).
+size_t ref_tiled_scale_bytes(int dim, int K, int group, int subs) {
+    int group_pad = (group + 3) / 4 * 4;
+    return (size_t)(dim / 32 / group) * (size_t)(K / 64 / subs) * 64 * subs * group_pad;
+}
+void ref_tile_scales(const uint8_t* raw, int dim, int K, int group, int subs, uint8_t* out) {
+    TiledScale ts = tile_scale(preprocess_scale(raw, dim, K), group, subs);
+    std::memcpy(out, ts.data.data(), ts.data.size());
 }
 
 // A: packed [M][3K/4] + raw scales [M][K/32]; Bt: packed [N][3K/4] + scales [N][K/32].

@@ -101,6 +101,19 @@ def main() -> None:
     out["gemmq_A"], out["gemmq_sA"], out["gemmq_Bt"], out["gemmq_sB"] = A2, sA2, B2, sB2
     out["gemmq_D"] = ref.gemm(A2, sA2, B2, sB2, K2)
 
+    # Reference device layouts (gfx950) for the import path: preshuffle_B and tile_scale with the
+    # reference's K_TILE = 192 (subs = 3) and its route groupings, on a small K = 384 problem.
+    N3, K3 = 256, 384
+    b3 = rng.uniform(-1, 1, (N3, K3)).astype(np.float32)
+    B3, sB3 = ref.quantize(b3)
+    a3 = rng.uniform(-1, 1, (128, K3)).astype(np.float32)
+    A3, sA3 = ref.quantize(a3)
+    out["imp_Bt"], out["imp_sB"], out["imp_A"], out["imp_sA"] = B3, sB3, A3, sA3
+    out["imp_Bsh"] = ref.preshuffle_B(B3, sB3, K3)
+    for grp in (2, 3, 4):
+        out[f"imp_sB_tiled_g{grp}"] = ref.tile_scales(sB3, N3, K3, grp, 3) if (N3 // 32) % grp == 0 else np.zeros(0, np.uint8)
+        out[f"imp_sA_tiled_g{grp}"] = ref.tile_scales(sA3, 128, K3, grp, 3) if (128 // 32) % grp == 0 else np.zeros(0, np.uint8)
+
     path = os.path.join(HERE, "golden.npz")
     np.savez_compressed(path, **out)
     print(f"wrote {path} ({os.path.getsize(path)} bytes, {len(out)} arrays)")
