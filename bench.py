@@ -252,7 +252,7 @@ def run_ours(args):
     sB = torch.from_numpy(lib.preprocess_scale(b_ops.sB, N, Kp)).to(dev)
     tdt = {lib.OutType.F32: torch.float32, lib.OutType.F16: torch.float16, lib.OutType.BF16: torch.bfloat16}[ot]
     D = torch.empty((M, N), dtype=tdt, device=dev)
-    wsb = lib.gemm_workspace_size(M, N, Kp)
+    wsb = lib.gemm_workspace_size(M, N, Kp, ot)  # this output type's split (the type-free query is the max)
     ws = torch.empty(max(wsb, 16), dtype=torch.uint8, device=dev)
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
     stream = torch.cuda.current_stream(dev)

@@ -7,8 +7,9 @@
 // It is the step before the GEMM for activations (the FFN's A operand), so it writes the scales
 // either raw [rows][cols/32] or directly in the GEMM's 128x4 atom layout.
 //
-// HBM bound: each element reads 4 bytes and writes 0.75 + 1/32. One warp quantises four blocks
-// (128 elements, one float4 per lane) and writes its 96 packed bytes as 24 aligned words.
+// HBM bound: each element reads 4 bytes and writes 0.75 + 1/32. A warp quantises 128-element
+// chunks (four blocks, one float4 per lane), four chunks per warp with their loads in flight
+// together, and writes each chunk's 96 packed bytes as 24 aligned words.
 #include <cuda_runtime.h>
 
 #include <atomic>
@@ -41,56 +42,40 @@ __device__ __forceinline__ uint32_t ceil_pow2_code(float v) {
     return (uint32_t)(code < 0 ? 0 : (code > 254 ? 254 : code));
 }
 
-// Nearest integer of q >= 0 (exactly representable), ties to even.
-__device__ __forceinline__ int rne(float q) {
-    const float f = floorf(q);
-    const float d = q - f;
-    const int b = (int)f;
-    return d > 0.5f ? b + 1 : (d < 0.5f ? b : b + (b & 1));
-}
-
+// Nearest E2M3 code, ties to even, saturating at 7.5, from the float's bits. Below 1.0 the grid
+// is 1/8 (an exact *8 and round-half-even); from 1.0 to 7.5 the 23-bit mantissa is rounded to 3
+// bits, and a mantissa carry moves into the exponent field by plain addition. Same results as
+// the reference's conversion (include/mxfp6/types.hpp:26-72), NaN -> 0x18 included.
 __device__ __forceinline__ uint32_t to_e2m3(float v) {
-    uint32_t s = 0;
-    if (v < 0.0f) {
-        s = 0x20;
-        v = -v;
+    const uint32_t b = __float_as_uint(v);
+    const uint32_t a = b & 0x7FFFFFFFu;
+    if (a > 0x7F800000u) return 0x18;                  // NaN
+    const uint32_t sgn = v < 0.0f ? 0x20u : 0u;        // -0.0 keeps code 0
+    uint32_t code;
+    if (a >= 0x40F00000u) {                            // >= 7.5 (Inf included): saturate
+        code = 0x1F;
+    } else if (a < 0x3F800000u) {                      // < 1.0: subnormal grid of 1/8
+        code = (uint32_t)__float2int_rn(__uint_as_float(a) * 8.0f);  // 0..8; 8 is the code of 1.0
+    } else {
+        const uint32_t ex = (a >> 23) - 127u;          // 0, 1 or 2
+        const uint32_t man = a & 0x7FFFFFu;
+        const uint32_t m3 = (man + 0x7FFFFu + ((man >> 20) & 1u)) >> 20;  // 0..8
+        code = ((ex + 1u) << 3) + m3;
     }
-    if (v == 0.0f) return s;
-    if (v != v) return 0x18;
-    if (v > 7.5f) v = 7.5f;
-    if (v < 1.0f) {
-        const int m = rne(v * 8.0f);
-        return m <= 0 ? s : (m >= 8 ? (s | 0x08) : (s | (uint32_t)m));
-    }
-    int e = v < 2.0f ? 1 : (v < 4.0f ? 2 : 3);
-    const float frac = v / (float)(1 << (e - 1)) - 1.0f;
-    int m = rne(frac * 8.0f);
-    if (m >= 8) {
-        m = 0;
-        if (++e > 3) return s | 0x1F;
-    }
-    return s | ((uint32_t)e << 3) | (uint32_t)m;
+    return sgn | code;
 }
 
-// 2^(code - 127) from the bits (code 0 is the subnormal 2^-127; code 255 never occurs here).
-__device__ __forceinline__ float e8m0_value(uint32_t code) {
-    return code == 0 ? __int_as_float(0x00400000) : __int_as_float((int)(code << 23));
+// 1 / 2^(code - 127) = 2^(127 - code), exact for every code the quantiser produces (0..254):
+// multiplying by it rounds exactly like dividing by the scale.
+__device__ __forceinline__ float e8m0_reciprocal(uint32_t code) {
+    const int e = 254 - (int)code;  // biased exponent of 2^(127 - code)
+    return e > 0 ? __int_as_float(e << 23) : __int_as_float(0x00400000 >> (-e));
 }
 
-// grid: x = 128-element chunks of a row, y = rows (blockDim 32, one warp per chunk)
-__global__ void __launch_bounds__(256) quantize_kernel(const float* __restrict__ in, int rows, int cols,
-                                                       uint8_t* __restrict__ packed, uint8_t* __restrict__ scales,
-                                                       int tiled) {
-    const int lane = threadIdx.x & 31;
-    const int chunk = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);  // 128 columns each
-    const int row = blockIdx.y;
-    if (chunk * 128 >= cols || row >= rows) return;
-    const int col = chunk * 128 + 4 * lane;
-    const bool live = col < cols;  // cols % 32 == 0, so whole 8-lane blocks are live or not
-    float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (live) x = *reinterpret_cast<const float4*>(in + (size_t)row * cols + col);
-    // block max over 8 lanes; NaN never wins a > comparison
-    float m = 0.0f;
+// Quantise one 128-element chunk held as one float4 per lane; returns the packed word this lane
+// writes (lanes 0..23) and the block's scale code (valid in every lane of the block).
+__device__ __forceinline__ uint32_t quantize_chunk(float4 x, int lane, uint32_t& code) {
+    float m = 0.0f;  // block max over 8 lanes; NaN never wins a > comparison
     for (float a : {fabsf(x.x), fabsf(x.y), fabsf(x.z), fabsf(x.w)})
         if (a > m) m = a;
 #pragma unroll
@@ -98,31 +83,60 @@ __global__ void __launch_bounds__(256) quantize_kernel(const float* __restrict__
         const float o = __shfl_xor_sync(0xffffffffu, m, off);
         if (o > m) m = o;
     }
-    const uint32_t code = m == 0.0f ? 127u : ceil_pow2_code(__fdiv_rn(m, 7.5f));
-    const float sv = e8m0_value(code);
-    const uint32_t q0 = to_e2m3(__fdiv_rn(x.x, sv)), q1 = to_e2m3(__fdiv_rn(x.y, sv)),
-                   q2 = to_e2m3(__fdiv_rn(x.z, sv)), q3 = to_e2m3(__fdiv_rn(x.w, sv));
+    code = m == 0.0f ? 127u : ceil_pow2_code(__fdiv_rn(m, 7.5f));
+    const float inv = e8m0_reciprocal(code);
+    const uint32_t q0 = to_e2m3(x.x * inv), q1 = to_e2m3(x.y * inv), q2 = to_e2m3(x.z * inv),
+                   q3 = to_e2m3(x.w * inv);
     const uint32_t g = q0 | (q1 << 6) | (q2 << 12) | (q3 << 18);  // this lane's 3 bytes
-    // Bytes [3*lane, 3*lane + 3) of the warp's 96; lane w < 24 writes word w = bytes [4w, 4w + 4).
-    const int lo = (4 * lane) / 3, hi = (4 * lane + 3) / 3;
+    // Bytes [3*lane, 3*lane + 3) of the chunk's 96; lane w < 24 packs word w = bytes [4w, 4w + 4).
+    const int lo = (4 * lane) / 3;
     const uint32_t glo = __shfl_sync(0xffffffffu, g, lo & 31);
-    const uint32_t ghi = __shfl_sync(0xffffffffu, g, hi & 31);
+    const uint32_t ghi = __shfl_sync(0xffffffffu, g, (lo + 1) & 31);
     const int sh = 4 * lane - 3 * lo;  // byte offset of word w inside lane lo's 3 bytes (0..2)
-    const uint32_t word = (glo >> (8 * sh)) | (ghi << (8 * (3 - sh)));
+    return (glo >> (8 * sh)) | (ghi << (8 * (3 - sh)));
+}
+
+// One warp per (row, group of CHUNKS consecutive 128-element chunks); all loads of the group are
+// issued before any is used. Grid: x covers the chunk groups of a row, y the rows.
+constexpr int CHUNKS = 4;
+
+__global__ void __launch_bounds__(256) quantize_kernel(const float* __restrict__ in, int rows, int cols,
+                                                       uint8_t* __restrict__ packed, uint8_t* __restrict__ scales,
+                                                       int tiled) {
+    const int lane = threadIdx.x & 31;
+    const int group = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int row = blockIdx.y;
+    const int chunk0 = group * CHUNKS;
+    if (chunk0 * 128 >= cols || row >= rows) return;
+    const float* src = in + (size_t)row * cols;
+    float4 x[CHUNKS];
+#pragma unroll
+    for (int c = 0; c < CHUNKS; c++) {
+        const int col = (chunk0 + c) * 128 + 4 * lane;
+        x[c] = col < cols ? __ldcs(reinterpret_cast<const float4*>(src + col)) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
     const int row_bytes = cols / 4 * 3;
-    const int valid = min(96, row_bytes - chunk * 96);  // a multiple of 24 (cols % 32 == 0)
-    if (lane < 24 && 4 * lane < valid)
-        *reinterpret_cast<uint32_t*>(packed + (size_t)row * row_bytes + chunk * 96 + 4 * lane) = word;
-    if (live && (lane & 7) == 0) {
-        const int j = col / 32;  // block index in the row
-        size_t off;
-        if (tiled) {
-            const size_t atom = (size_t)(row / 128) * (size_t)(cols / 128) + (size_t)(j / 4);
-            off = atom * 512 + (size_t)((row % 32) * 16 + ((row % 128) / 32) * 4 + (j % 4));
-        } else {
-            off = (size_t)row * (cols / 32) + j;
+#pragma unroll
+    for (int c = 0; c < CHUNKS; c++) {
+        const int chunk = chunk0 + c;
+        if (chunk * 128 >= cols) break;  // uniform across the warp
+        uint32_t code;
+        const uint32_t word = quantize_chunk(x[c], lane, code);
+        const int valid = min(96, row_bytes - chunk * 96);  // a multiple of 24 (cols % 32 == 0)
+        if (lane < 24 && 4 * lane < valid)
+            *reinterpret_cast<uint32_t*>(packed + (size_t)row * row_bytes + chunk * 96 + 4 * lane) = word;
+        const int col = chunk * 128 + 4 * lane;
+        if (col < cols && (lane & 7) == 0) {
+            const int j = col / 32;  // block index in the row
+            size_t off;
+            if (tiled) {
+                const size_t atom = (size_t)(row / 128) * (size_t)(cols / 128) + (size_t)(j / 4);
+                off = atom * 512 + (size_t)((row % 32) * 16 + ((row % 128) / 32) * 4 + (j % 4));
+            } else {
+                off = (size_t)row * (cols / 32) + j;
+            }
+            scales[off] = (uint8_t)code;
         }
-        scales[off] = (uint8_t)code;
     }
 }
 
@@ -147,7 +161,8 @@ extern "C" int mxfp6_quantize_device(const float* d_mat, int rows, int cols, uin
         return MXFP6_ERR_INVALID_SHAPE;
     }
     const int chunks = (cols + 127) / 128;
-    dim3 grid((chunks + 7) / 8, rows);
+    const int groups = (chunks + CHUNKS - 1) / CHUNKS;
+    dim3 grid((groups + 7) / 8, rows);
     quantize_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(d_mat, rows, cols, d_packed, d_scales,
                                                                         scale_layout);
     cudaError_t e = cudaGetLastError();

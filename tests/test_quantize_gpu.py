@@ -64,3 +64,26 @@ def test_matches_host_tiled_scales(lib, rows, cols):
     p, s = _device_quantize(lib, m, tiled=True)
     assert np.array_equal(p, host.packed_data)
     assert np.array_equal(s, lib.preprocess_scale(host.scales, rows, cols))
+
+
+def test_every_golden_encode_input(lib, golden):
+    """Blocks whose max is exactly 7.5 get scale 2^0, so each code is the E2M3 conversion of the
+    input itself: every golden encode input with |x| <= 7.5 (and NaN) goes through the device."""
+    xs = golden["fp6_encode_in"]
+    want = golden["fp6_encode_out"]
+    keep = np.isnan(xs) | (np.abs(xs) <= 7.5)
+    xs, want = xs[keep], want[keep]
+    per = 31
+    nblk = (len(xs) + per - 1) // per
+    vals = np.zeros(nblk * per, np.float32)
+    vals[:len(xs)] = xs
+    blocks = np.concatenate([np.full((nblk, 1), 7.5, np.float32), vals.reshape(nblk, per)], axis=1)
+    rows = (nblk + 3) // 4
+    m = np.zeros((rows * 4, 32), np.float32)
+    m[:nblk] = blocks
+    m = m.reshape(rows, 128)
+    p, s = _device_quantize(lib, m, tiled=False)
+    assert (s[:nblk] == 127).all()
+    codes = lib.unpack_codes(p).reshape(-1, 32)[:nblk, 1:].reshape(-1)[:len(xs)]
+    bad = np.nonzero(codes != want)[0]
+    assert bad.size == 0, f"{bad.size} mismatches, first inputs {xs[bad[:5]]}"
