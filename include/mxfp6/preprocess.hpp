@@ -31,10 +31,11 @@ namespace mxfp6 {
 
 // ---- K padding: the "pad B only / compact A" recipe -----------------------------------------
 // B (weights) is padded offline to kpad(K) with a zero K-tail; A may keep its compact layout
-// (row stride fp6_packed_bytes(K)), reading past each row into the next, provided the buffer
-// has a_compact_end_pad(K) spare bytes and A's scales are extended with a finite tail.
-// On B200 the tensor-memory accelerator needs 32-byte row strides, so compact A with
-// K % 128 != 0 is rejected by gemm(); pad A to kpad(K) for those shapes.
+// (row stride A_row_bytes = fp6_packed_bytes(K)) provided A's scales are extended with a finite
+// tail (pad_scales_k). The tensor-memory accelerator cannot address such a stride (it needs a
+// multiple of 32 bytes), so gemm() loads compact A with the kernels' software producer, which
+// zero-fills each row's K tail instead of reading into the next row: the end pad below is
+// accepted but never read.
 inline int a_compact_end_pad(int K) {
     return fp6_packed_bytes(kpad(K)) - fp6_packed_bytes(K);
 }

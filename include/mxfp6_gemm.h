@@ -144,6 +144,13 @@ void mxfp6_quantize(const float* mat, int rows, int cols, uint8_t* packed, uint8
 int mxfp6_quantize_device(const float* d_mat, int rows, int cols, uint8_t* d_packed, uint8_t* d_scales,
                           int scale_layout, void* stream);
 
+/* The same, writing rows of padded_cols codes (3*padded_cols/4 bytes, zero tail) and scales for
+ * padded_cols/32 blocks (tail blocks get the finite code 127): activations quantised this way
+ * meet the GEMM's 32-byte row-stride rule for any K with K % 32 == 0 (use padded_cols = kpad(K)).
+ * No counterpart in the reference, whose "compact A" recipe reads rows of K codes in place. */
+int mxfp6_quantize_device_padded(const float* d_mat, int rows, int cols, int padded_cols, uint8_t* d_packed,
+                                 uint8_t* d_scales, int scale_layout, void* stream);
+
 /* dequantize_mxfp6 (reference: include/mxfp6/preprocess.hpp:100-109). */
 void mxfp6_dequantize(const uint8_t* packed, const uint8_t* scales, int rows, int cols,
                       float* out);
@@ -173,6 +180,13 @@ int mxfp6_import_ref_B(const uint8_t* ref_bsh, int N, int Kp_ref, uint8_t* out, 
  * (include/mxfp6/preprocess.hpp:136-162,216-233): writes raw scales [dim][Kp_ref/32]. group is
  * the reference's MPW/NPW for the route it tiled for, subs its K_TILE/64 (3). */
 int mxfp6_import_ref_scales(const uint8_t* ref_tiled, int dim, int Kp_ref, int group, int subs, uint8_t* raw_out);
+
+/* Device version of mxfp6_repad_rows (device pointers, asynchronous on `stream`): turns an A
+ * operand in the reference's compact layout (row stride 3*K/4 with K % 128 != 0, which the
+ * tensor-memory accelerator cannot address) into rows of 3*kpad(K)/4 bytes in a caller buffer;
+ * pair it with pad_scales_k / mxfp6_tile_scales for the scales. */
+int mxfp6_repad_rows_device(const void* d_src, int rows, int src_row_bytes, int bytes_used, void* d_dst,
+                            int dst_row_bytes, void* stream);
 
 /* Copy rows of src_bytes_used bytes from a src_row_bytes stride to a dst_row_bytes stride,
  * zero-filling each row's tail (re-padding A rows from the reference's Kp to this library's). */

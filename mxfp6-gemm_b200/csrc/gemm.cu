@@ -124,6 +124,20 @@ bool aligned(const void* p, uintptr_t a) {
     return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0;
 }
 
+// A operands the tensor-memory accelerator can read: stride a multiple of 32 bytes, at least the
+// packed Kp codes, 32-byte aligned base. Other A operands go through the software producer
+// (compact_a.cuh) when their stride is a multiple of 4 bytes and holds the row's real K codes:
+// 0.75*Kp - 96 < A_row_bytes, i.e. kpad(4*A_row_bytes/3) == Kp — the reference's compact-A
+// recipe (row stride 3K/4) is exactly this case.
+bool a_uses_tma(int Kp, const void* dA, int A_row_bytes) {
+    return A_row_bytes % 32 == 0 && (long long)A_row_bytes >= (long long)Kp * 3 / 4 && aligned(dA, 32);
+}
+
+// Producer for A: the 16U6 tensor load, or the loader warps' 4-byte cp.async copies.
+int a_mode(int Kp, const void* dA, int A_row_bytes) {
+    return a_uses_tma(Kp, dA, A_row_bytes) ? kern::A_TMA : kern::A_CPASYNC;
+}
+
 bool validate(int ot, int M, int N, int Kp, const void* dA, const void* dB, const void* sA,
               const void* sB, const void* dD, int A_row_bytes, int B_row_bytes) {
     if (ot < MXFP6_OUT_F32 || ot > MXFP6_OUT_BF16) {
@@ -138,11 +152,18 @@ bool validate(int ot, int M, int N, int Kp, const void* dA, const void* dB, cons
         return false;
     }
     const long long need = (long long)Kp * 3 / 4;
-    if (A_row_bytes < need || B_row_bytes < need || A_row_bytes % 32 || B_row_bytes % 32) {
+    if (B_row_bytes < need || B_row_bytes % 32) {
         set_error(MXFP6_ERR_INVALID_STRIDE,
-                  "row strides A=%d B=%d bytes: each must be >= %lld (= 0.75*Kp) and a multiple of "
-                  "32 for the tensor-memory accelerator's FP6 unpack mode",
-                  A_row_bytes, B_row_bytes, need);
+                  "B row stride %d bytes: must be >= %lld (= 0.75*Kp) and a multiple of 32 for the "
+                  "tensor-memory accelerator's FP6 unpack mode (pad B to Kp)",
+                  B_row_bytes, need);
+        return false;
+    }
+    if (A_row_bytes % 4 || A_row_bytes <= need - 96) {
+        set_error(MXFP6_ERR_INVALID_STRIDE,
+                  "A row stride %d bytes: must be a multiple of 4 and hold the row's K codes "
+                  "(> %lld = 0.75*Kp - 96; the compact stride 3K/4 of any K with kpad(K) == Kp)",
+                  A_row_bytes, need - 96);
         return false;
     }
     if (!dA || !dB || !sA || !sB || !dD) {
@@ -150,9 +171,10 @@ bool validate(int ot, int M, int N, int Kp, const void* dA, const void* dB, cons
                   sA, sB, dD);
         return false;
     }
-    if (!aligned(dA, 32) || !aligned(dB, 32) || !aligned(sA, 16) || !aligned(sB, 16) || !aligned(dD, 16)) {
+    if (!aligned(dA, 4) || !aligned(dB, 32) || !aligned(sA, 16) || !aligned(sB, 16) || !aligned(dD, 16)) {
         set_error(MXFP6_ERR_MISALIGNED,
-                  "misaligned pointer: A and B need 32-byte, scales and D 16-byte alignment");
+                  "misaligned pointer: A needs 4-byte (32-byte for the tensor-load path), B 32-byte, "
+                  "scales and D 16-byte alignment");
         return false;
     }
     return true;
@@ -160,12 +182,27 @@ bool validate(int ot, int M, int N, int Kp, const void* dA, const void* dB, cons
 
 // ---- launch ----------------------------------------------------------------------------------------
 
-template <int BN, typename OutT, bool PARTIAL>
+// Compact-A fields of the kernel parameters (unused on the tensor-load path).
+void set_compact(kern::Params& p, int Kp, const void* dA, int A_row_bytes) {
+    p.a_ptr = static_cast<const uint8_t*>(dA);
+    p.a_stride = A_row_bytes;
+    const int need = Kp / 4 * 3;
+    p.a_valid = A_row_bytes < need ? A_row_bytes : need;
+}
+
+// A tensor map for the 16U6 tensor load (unused, zeroed, by the loader-warp producers).
+bool make_a_tmap(int amode, CUtensorMap* map, const void* dA, int M, int Kp, int A_row_bytes, int box_rows) {
+    std::memset(map, 0, sizeof(*map));
+    if (amode == kern::A_TMA) return make_fp6_tmap(map, dA, M, Kp, A_row_bytes, box_rows);
+    return true;
+}
+
+template <int BN, typename OutT, bool PARTIAL, int AMODE>
 bool launch_gemm(int M, int N, int Kp, const void* dA, const void* dB, const uint8_t* sA,
                  const uint8_t* sB, void* dD, float* ws, int A_row_bytes, int B_row_bytes, int splits,
                  cudaStream_t stream) {
-    using C = kern::Config<BN>;
-    auto kernel = kern::gemm_mxfp6_sm100<BN, OutT, PARTIAL>;
+    using C = kern::Config<BN, AMODE>;
+    auto kernel = kern::gemm_mxfp6_sm100<BN, OutT, PARTIAL, AMODE>;
     static std::once_flag attr_once[kMaxDevices];
     const int dev = current_device();
     if (dev < 0 || dev >= kMaxDevices) {
@@ -181,7 +218,7 @@ bool launch_gemm(int M, int N, int Kp, const void* dA, const void* dB, const uin
         return false;
     }
     CUtensorMap tmA, tmB;
-    if (!make_fp6_tmap(&tmA, dA, M, Kp, A_row_bytes, kern::BM) ||
+    if (!make_a_tmap(AMODE, &tmA, dA, M, Kp, A_row_bytes, kern::BM) ||
         !make_fp6_tmap(&tmB, dB, N, Kp, B_row_bytes, BN)) {
         set_error(MXFP6_ERR_CUDA, "cuTensorMapEncodeTiled failed for %dx%dx%d", M, N, Kp);
         return false;
@@ -199,9 +236,10 @@ bool launch_gemm(int M, int N, int Kp, const void* dA, const void* dB, const uin
     p.k_slabs = Kp / kern::BK;
     p.splits = splits;
     p.out_align32 = aligned(PARTIAL ? static_cast<const void*>(ws) : dD, 32) ? 1 : 0;
+    set_compact(p, Kp, dA, A_row_bytes);
     const long long tiles = (long long)p.m_blocks * p.n_blocks * splits;
     const int grid = (int)(tiles < sm_count() ? tiles : sm_count());
-    kernel<<<grid, kern::NUM_THREADS, C::SMEM_BYTES, stream>>>(tmA, tmB, p);
+    kernel<<<grid, kern::threads_for(AMODE), C::SMEM_BYTES, stream>>>(tmA, tmB, p);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) {
         set_error(MXFP6_ERR_CUDA, "GEMM launch failed: %s", cudaGetErrorString(e));
@@ -211,11 +249,11 @@ bool launch_gemm(int M, int N, int Kp, const void* dA, const void* dB, const uin
     return true;
 }
 
-template <typename OutT, bool PARTIAL>
+template <typename OutT, bool PARTIAL, int AMODE>
 bool launch_pair(int M, int N, int Kp, const void* dA, const void* dB, const uint8_t* sA, const uint8_t* sB,
                  void* dD, float* ws, int A_row_bytes, int B_row_bytes, int splits, cudaStream_t stream) {
-    using C = kern::PairConfig;
-    auto kernel = kern::gemm_mxfp6_sm100_pair<OutT, PARTIAL>;
+    using C = kern::PairConfig<AMODE>;
+    auto kernel = kern::gemm_mxfp6_sm100_pair<OutT, PARTIAL, AMODE>;
     static std::once_flag attr_once[kMaxDevices];
     const int dev = current_device();
     if (dev < 0 || dev >= kMaxDevices) {
@@ -231,7 +269,7 @@ bool launch_pair(int M, int N, int Kp, const void* dA, const void* dB, const uin
         return false;
     }
     CUtensorMap tmA, tmB, tmSA, tmSB;
-    if (!make_fp6_tmap(&tmA, dA, M, Kp, A_row_bytes, 128) || !make_fp6_tmap(&tmB, dB, N, Kp, B_row_bytes, 128) ||
+    if (!make_a_tmap(AMODE, &tmA, dA, M, Kp, A_row_bytes, 128) || !make_fp6_tmap(&tmB, dB, N, Kp, B_row_bytes, 128) ||
         !make_sf_tmap(&tmSA, sA, M, Kp, 1, C::SUB) || !make_sf_tmap(&tmSB, sB, N, Kp, 2, C::SUB)) {
         set_error(MXFP6_ERR_CUDA, "cuTensorMapEncodeTiled failed for %dx%dx%d", M, N, Kp);
         return false;
@@ -249,12 +287,13 @@ bool launch_pair(int M, int N, int Kp, const void* dA, const void* dB, const uin
     p.k_slabs = Kp / kern::BK;
     p.splits = splits;
     p.out_align32 = aligned(PARTIAL ? static_cast<const void*>(ws) : dD, 32) ? 1 : 0;
+    set_compact(p, Kp, dA, A_row_bytes);
     const long long units = (long long)p.m_blocks * p.n_blocks * splits;
     const int pairs = sm_count() / 2;
     const int clusters = (int)(units < pairs ? units : pairs);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * clusters, 1, 1);
-    cfg.blockDim = dim3(kern::NUM_THREADS, 1, 1);
+    cfg.blockDim = dim3(kern::threads_for(AMODE), 1, 1);
     cfg.dynamicSmemBytes = C::SMEM_BYTES;
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
@@ -291,23 +330,35 @@ bool launch_reduce(const float* ws, void* dD, int M, int N, int splits, cudaStre
     return true;
 }
 
-template <typename OutT>
-bool run_typed(const Route& r, int M, int N, int Kp, const void* dA, const void* dB, const uint8_t* sA,
+// Partial (split-K) launches write FP32 whatever the output type, so they share the float
+// instantiation; the reduce pass converts.
+template <typename OutT, int AMODE>
+bool run_route(const Route& r, int M, int N, int Kp, const void* dA, const void* dB, const uint8_t* sA,
                const uint8_t* sB, void* dD, int Ar, int Br, void* ws, cudaStream_t stream) {
     float* wsf = static_cast<float*>(ws);
     const bool part = r.splits > 1;
     bool ok;
     if (r.MT == 256) {
-        ok = part ? launch_pair<OutT, true>(M, N, Kp, dA, dB, sA, sB, dD, wsf, Ar, Br, r.splits, stream)
-                  : launch_pair<OutT, false>(M, N, Kp, dA, dB, sA, sB, dD, wsf, Ar, Br, 1, stream);
+        ok = part ? launch_pair<float, true, AMODE>(M, N, Kp, dA, dB, sA, sB, dD, wsf, Ar, Br, r.splits, stream)
+                  : launch_pair<OutT, false, AMODE>(M, N, Kp, dA, dB, sA, sB, dD, wsf, Ar, Br, 1, stream);
     } else if (r.NT == 256) {
-        ok = part ? launch_gemm<256, OutT, true>(M, N, Kp, dA, dB, sA, sB, dD, wsf, Ar, Br, r.splits, stream)
-                  : launch_gemm<256, OutT, false>(M, N, Kp, dA, dB, sA, sB, dD, wsf, Ar, Br, 1, stream);
+        ok = part ? launch_gemm<256, float, true, AMODE>(M, N, Kp, dA, dB, sA, sB, dD, wsf, Ar, Br, r.splits,
+                                                           stream)
+                  : launch_gemm<256, OutT, false, AMODE>(M, N, Kp, dA, dB, sA, sB, dD, wsf, Ar, Br, 1, stream);
     } else {
-        ok = part ? launch_gemm<128, OutT, true>(M, N, Kp, dA, dB, sA, sB, dD, wsf, Ar, Br, r.splits, stream)
-                  : launch_gemm<128, OutT, false>(M, N, Kp, dA, dB, sA, sB, dD, wsf, Ar, Br, 1, stream);
+        ok = part ? launch_gemm<128, float, true, AMODE>(M, N, Kp, dA, dB, sA, sB, dD, wsf, Ar, Br, r.splits,
+                                                           stream)
+                  : launch_gemm<128, OutT, false, AMODE>(M, N, Kp, dA, dB, sA, sB, dD, wsf, Ar, Br, 1, stream);
     }
     return ok && (!part || launch_reduce<OutT>(wsf, dD, M, N, r.splits, stream));
+}
+
+template <typename OutT>
+bool run_typed(const Route& r, int M, int N, int Kp, const void* dA, const void* dB, const uint8_t* sA,
+               const uint8_t* sB, void* dD, int Ar, int Br, void* ws, cudaStream_t stream) {
+    return a_mode(Kp, dA, Ar) == kern::A_TMA
+               ? run_route<OutT, kern::A_TMA>(r, M, N, Kp, dA, dB, sA, sB, dD, Ar, Br, ws, stream)
+               : run_route<OutT, kern::A_CPASYNC>(r, M, N, Kp, dA, dB, sA, sB, dD, Ar, Br, ws, stream);
 }
 
 bool run(int ot, const Route& r, int M, int N, int Kp, const void* dA, const void* dB, const uint8_t* sA,

@@ -32,6 +32,7 @@
 #include <cstdint>
 #include <type_traits>
 
+#include "compact_a.cuh"
 #include "sm100_ptx.cuh"
 
 namespace mxfp6 {
@@ -50,7 +51,7 @@ constexpr int EPI_WARP0 = 2;        // first epilogue warp
 constexpr int A_TMA_BYTES = BM * BK * 3 / 4;  // packed bytes one A slab moves
 constexpr long long WAIT_BUDGET = 4000000000LL;  // cycles (about 2 s at 1.9 GHz)
 
-template <int BN>
+template <int BN, int AMODE = A_TMA>
 struct Config {
     static_assert(BN == 128 || BN == 256, "tile width");
     static constexpr int STAGES = BN == 256 ? 4 : 6;
@@ -78,6 +79,9 @@ struct Params {
     int M, N, Kp;
     int m_blocks, n_blocks, k_slabs, splits;
     int out_align32;  // D (or ws in partial mode) is 32-byte aligned: 256-bit stores
+    // compact A (software producer, compact_a.cuh): packed rows, stride and valid bytes per row
+    const uint8_t* a_ptr;
+    int a_stride, a_valid;
 };
 
 struct TileCoord {
@@ -160,11 +164,14 @@ __device__ __forceinline__ void store_row_chunk<__nv_bfloat16>(__nv_bfloat16* ds
 }
 
 // OutT: float / __half / __nv_bfloat16. PARTIAL: write FP32 partial sums to p.ws instead of D.
-template <int BN, typename OutT, bool PARTIAL>
-__global__ void __launch_bounds__(NUM_THREADS, 1)
+// AMODE (compact_a.cuh): A_TMA loads A with the 16U6 tensor load; A_CPASYNC adds four
+// loader warps that copy the A image from p.a_ptr (tmA unused).
+template <int BN, typename OutT, bool PARTIAL, int AMODE = A_TMA>
+__global__ void __launch_bounds__(threads_for(AMODE), 1)
     gemm_mxfp6_sm100(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      const Params p) {
-    using C = Config<BN>;
+    using C = Config<BN, AMODE>;
+    constexpr bool COMPACT = AMODE != A_TMA;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     // 1024-byte alignment for the 128-byte-swizzled operand tiles.
     const uint32_t raw_u32 = sm100::smem_u32(smem_raw);
@@ -181,15 +188,17 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     const uint32_t acc_full = bar_base + 8u * (2 * C::STAGES);
     const uint32_t acc_empty = acc_full + 8u;
     const uint32_t drain_bar = acc_full + 16u;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_ptr + 8 * (2 * C::STAGES + 3));
-    volatile int* abort_flag = reinterpret_cast<volatile int*>(bar_ptr + 8 * (2 * C::STAGES + 3) + 8);
+    const int slot_off = 8 * (2 * C::STAGES + 3);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_ptr + slot_off);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(bar_ptr + slot_off + 8);
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < C::STAGES; s++) {
-            sm100::mbar_init(full_bar(s), 1);
+            // producer, plus one arrival per loader thread (A_CPASYNC)
+            sm100::mbar_init(full_bar(s), AMODE == A_CPASYNC ? 1 + LOADER_THREADS : 1);
             sm100::mbar_init(empty_bar(s), 1);
         }
         sm100::mbar_init(acc_full, 1);
@@ -198,9 +207,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         *abort_flag = 0;
         sm100::fence_mbar_init();
         sm100::fence_async_shared();
-        sm100::prefetch_tmap(&tmA);
+        if (AMODE == A_TMA) sm100::prefetch_tmap(&tmA);
         sm100::prefetch_tmap(&tmB);
     }
+
     if (warp == 1) {
         sm100::tmem_alloc(sm100::smem_u32(tmem_slot), C::TMEM_COLS);
         sm100::tmem_relinquish();
@@ -225,10 +235,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 #pragma unroll
                 for (int j = 0; j < C::SFB_ATOMS; j++)
                     if (tc.nb * BN + j * 128 < p.N) sfb_atoms++;
-                const uint32_t tx = A_TMA_BYTES + C::B_TMA_BYTES + 512u * (1 + sfb_atoms);
+                const uint32_t tx = (COMPACT ? 0u : (uint32_t)A_TMA_BYTES) + C::B_TMA_BYTES + 512u * (1 + sfb_atoms);
                 for (int i = 0; i < tc.kb_count; i++) {
-                    if (!sm100::wait_parity_bounded(empty_bar(stage), phase ^ 1u, abort_flag,
-                                                    WAIT_BUDGET)) {
+                    if (!sm100::wait_parity_bounded(empty_bar(stage), phase ^ 1u, abort_flag, WAIT_BUDGET)) {
                         if (!*abort_flag) raise_status(0x1u, abort_flag);
                         ok = false;
                         break;
@@ -237,7 +246,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                     const uint32_t fb = full_bar(stage);
                     sm100::mbar_arrive_expect_tx(fb, tx);
                     const uint32_t a_dst = ab_base + stage * C::AB_STAGE;
-                    sm100::tma_load_2d(a_dst, &tmA, fb, kb * BK, tc.mb * BM);
+                    if (!COMPACT) sm100::tma_load_2d(a_dst, &tmA, fb, kb * BK, tc.mb * BM);
                     sm100::tma_load_2d(a_dst + C::A_BYTES, &tmB, fb, kb * BK, tc.nb * BN);
                     const uint32_t sf_dst = sf_base + stage * C::SF_STAGE;
                     sm100::bulk_load(sf_dst, p.sfA + ((size_t)tc.mb * p.k_slabs + kb) * 512, 512, fb);
@@ -253,7 +262,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                     }
                 }
             }
-            if (!ok) {
+            if (!ok && COMPACT) {
+                // The full barriers also count loader arrivals that may never come: give the
+                // tensor loads in flight time to land instead.
+                sm100::settle_ns(200000);
+            } else if (!ok) {
                 // Let every load still in flight land before shared memory is released.
                 const int zero = 0;
                 for (int s = 0; s < C::STAGES; s++)
@@ -322,6 +335,35 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                     atomicOr(&g_device_status, 0x8u);
             }
         }
+    } else if (AMODE == A_CPASYNC && warp >= LOADER_WARP0) {
+        // ---------------- A loader (A_CPASYNC, warps 6..9) ----------------
+        const int lt = threadIdx.x - 32 * LOADER_WARP0;
+        const CompactA a{p.a_ptr, p.a_stride, p.a_valid};
+        int stage = 0;
+        uint32_t phase = 0;
+        bool ok = true;
+        for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
+            const TileCoord tc = decode_tile(t, p);
+            for (int i = 0; i < tc.kb_count; i++) {
+                int got = 1;
+                if (lane == 0)
+                    got = sm100::wait_parity_bounded(empty_bar(stage), phase ^ 1u, abort_flag, WAIT_BUDGET) ? 1 : 0;
+                got = __shfl_sync(0xffffffffu, got, 0);
+                if (!got) {
+                    if (lane == 0 && !*abort_flag) raise_status(0x1u, abort_flag);
+                    ok = false;
+                    break;
+                }
+                sm100::mbar_try_wait(empty_bar(stage), phase ^ 1u);
+                compact_issue_slab(ab_base + stage * C::AB_STAGE, a, p.M, tc.mb * BM, tc.kb_begin + i, lt);
+                sm100::cp_async_mbar_arrive_noinc(full_bar(stage));
+                if (++stage == C::STAGES) {
+                    stage = 0;
+                    phase ^= 1u;
+                }
+            }
+        }
+        sm100::cp_async_wait_all();
     } else {
         // ---------------- epilogue (warps 2..5) ----------------
         const int quarter = warp & 3;  // tensor-memory lanes 32*quarter .. 32*quarter+31

@@ -28,6 +28,7 @@
 namespace mxfp6 {
 namespace kern {
 
+template <int AMODE = A_TMA>
 struct PairConfig {
     static constexpr int BM = 256;  // rows per pair tile (128 per CTA)
     static constexpr int BN = 256;  // columns per pair tile (B rows 128 per CTA)
@@ -58,21 +59,17 @@ __device__ __forceinline__ void store_cluster_u32(uint32_t cluster_addr, uint32_
     asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(cluster_addr), "r"(v) : "memory");
 }
 
-// Spin for about `ns` nanoseconds (bounded settle time on the abort path).
-__device__ __forceinline__ void settle_ns(unsigned long long ns) {
-    unsigned long long t0, t;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
-    do {
-        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-    } while (t - t0 < ns);
-}
-
-template <typename OutT, bool PARTIAL>
-__global__ void __launch_bounds__(NUM_THREADS, 1)
+// AMODE (compact_a.cuh): A_TMA loads A with the 16U6 tensor load; A_CPASYNC adds four
+// loader warps per CTA that build the A image from p.a_ptr, and whose arrivals join the leader's
+// full barrier.
+template <typename OutT, bool PARTIAL, int AMODE = A_TMA>
+__global__ void __launch_bounds__(threads_for(AMODE), 1)
     gemm_mxfp6_sm100_pair(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                           const __grid_constant__ CUtensorMap tmSA, const __grid_constant__ CUtensorMap tmSB,
                           const Params p) {
-    using C = PairConfig;
+    using C = PairConfig<AMODE>;
+    constexpr bool COMPACT = AMODE != A_TMA;
+    static_assert(!COMPACT || C::SUB == 1, "the compact-A loaders fill one 128-deep slab per stage");
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     const uint32_t raw_u32 = sm100::smem_u32(smem_raw);
     const uint32_t base = (raw_u32 + 1023u) & ~1023u;
@@ -106,7 +103,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < C::STAGES; s++) {
-            sm100::mbar_init(full_bar(s), 1);
+            // A_CPASYNC: leader = producer + own loader threads + the peer's relay; the peer's
+            // barrier counts its own loader threads.
+            uint32_t n = 1;
+            if (AMODE == A_CPASYNC) n = rank == 0 ? 2 + LOADER_THREADS : LOADER_THREADS;
+            sm100::mbar_init(full_bar(s), n);
             sm100::mbar_init(empty_bar(s), 1);
         }
         for (int b = 0; b < 2; b++) {
@@ -118,11 +119,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         *abort_flag = 0;
         sm100::fence_mbar_init();
         sm100::fence_async_shared();
-        sm100::prefetch_tmap(&tmA);
+        if (AMODE == A_TMA) sm100::prefetch_tmap(&tmA);
         sm100::prefetch_tmap(&tmB);
         sm100::prefetch_tmap(&tmSA);
         sm100::prefetch_tmap(&tmSB);
     }
+
     if (warp == 1) {
         sm100::tmem_alloc_pair(sm100::smem_u32(tmem_slot), C::TMEM_COLS);
         sm100::tmem_relinquish_pair();
@@ -157,10 +159,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                     const int kb = tc.kb_begin + i;
                     const int nsub = tc.kb_count - i < C::SUB ? tc.kb_count - i : C::SUB;
                     const uint32_t fb = sm100::mapa_shared(full_bar(stage), 0);
-                    if (rank == 0) sm100::mbar_arrive_expect_tx(full_bar(stage), C::tx_stage(nsub));
+                    if (rank == 0)
+                        sm100::mbar_arrive_expect_tx(full_bar(stage),
+                                                     C::tx_stage(nsub) - (COMPACT ? nsub * C::SLAB_TX : 0u));
                     const uint32_t a_dst = ab_base + stage * C::AB_STAGE;
                     for (int j = 0; j < nsub; j++) {
-                        sm100::tma_load_2d_pair(a_dst + j * C::SLAB_BYTES, &tmA, fb, (kb + j) * BK, a_row);
+                        if (!COMPACT)
+                            sm100::tma_load_2d_pair(a_dst + j * C::SLAB_BYTES, &tmA, fb, (kb + j) * BK, a_row);
                         sm100::tma_load_2d_pair(a_dst + C::A_BYTES + j * C::SLAB_BYTES, &tmB, fb, (kb + j) * BK,
                                                 b_row);
                     }
@@ -178,14 +183,16 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             }
             if (!ok) {
                 const int zero = 0;
-                if (rank == 0) {
+                if (rank == 0 && !COMPACT) {
                     for (int s = 0; s < C::STAGES; s++)
                         if ((issued_mask >> s) & 1u)
                             if (!sm100::wait_parity_bounded(full_bar(s), (issued_phase >> s) & 1u, &zero,
                                                                     WAIT_BUDGET / 4))
                                 atomicOr(&g_device_status, 0x8u);
                 } else {
-                    settle_ns(200000);  // the peer's loads report to the leader; give them time to land
+                    // the peer's loads report to the leader (and in compact mode the full barriers
+                    // also count loader arrivals that may never come): give them time to land
+                    sm100::settle_ns(200000);
                 }
             }
         }
@@ -263,7 +270,61 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 if (!sm100::wait_parity_bounded(drain_bar, 0, &zero, WAIT_BUDGET / 4))
                     atomicOr(&g_device_status, 0x8u);
             }
+        } else if (AMODE == A_CPASYNC && lane == 0) {
+            // ---------------- relay (peer only, A_CPASYNC) ----------------
+            // The peer's full barrier completes when its loaders' copies have landed; pass each
+            // completed phase on to the leader's full barrier of the same stage.
+            int stage = 0;
+            uint32_t phase = 0;
+            bool ok = true;
+            for (int t = cluster_id; t < total_tiles && ok; t += num_clusters) {
+                const TileCoord tc = decode_tile(t, p);
+                for (int i = 0; i < tc.kb_count; i++) {
+                    if (!sm100::wait_parity_bounded(full_bar(stage), phase, abort_flag, WAIT_BUDGET)) {
+                        if (!*abort_flag) raise(0x1u);
+                        ok = false;
+                        break;
+                    }
+                    sm100::mbar_arrive_cluster(sm100::mapa_shared(full_bar(stage), 0));
+                    if (++stage == C::STAGES) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+            }
         }
+    } else if (AMODE == A_CPASYNC && warp >= LOADER_WARP0) {
+        // ---------------- A loader (A_CPASYNC, warps 6..9 of both CTAs) ----------------
+        // Copies signal this CTA's own full barrier (a cp.async completion can only arrive on a
+        // barrier of its own CTA); the peer's relay forwards its barrier to the leader's.
+        const int lt = threadIdx.x - 32 * LOADER_WARP0;
+        const CompactA a{p.a_ptr, p.a_stride, p.a_valid};
+        int stage = 0;
+        uint32_t phase = 0;
+        bool ok = true;
+        for (int t = cluster_id; t < total_tiles && ok; t += num_clusters) {
+            const TileCoord tc = decode_tile(t, p);
+            const int a_row = tc.mb * C::BM + 128 * (int)rank;
+            for (int i = 0; i < tc.kb_count; i++) {
+                int got = 1;
+                if (lane == 0)
+                    got = sm100::wait_parity_bounded(empty_bar(stage), phase ^ 1u, abort_flag, WAIT_BUDGET) ? 1 : 0;
+                got = __shfl_sync(0xffffffffu, got, 0);
+                if (!got) {
+                    if (lane == 0 && !*abort_flag) raise(0x1u);
+                    ok = false;
+                    break;
+                }
+                sm100::mbar_try_wait(empty_bar(stage), phase ^ 1u);
+                compact_issue_slab(ab_base + stage * C::AB_STAGE, a, p.M, a_row, tc.kb_begin + i, lt);
+                sm100::cp_async_mbar_arrive_noinc(full_bar(stage));
+                if (++stage == C::STAGES) {
+                    stage = 0;
+                    phase ^= 1u;
+                }
+            }
+        }
+        sm100::cp_async_wait_all();
     } else {
         // ---------------- epilogue (warps 2..5 of both CTAs) ----------------
         const int quarter = warp & 3;

@@ -101,8 +101,8 @@ __device__ __forceinline__ uint32_t quantize_chunk(float4 x, int lane, uint32_t&
 constexpr int CHUNKS = 4;
 
 __global__ void __launch_bounds__(256) quantize_kernel(const float* __restrict__ in, int rows, int cols,
-                                                       uint8_t* __restrict__ packed, uint8_t* __restrict__ scales,
-                                                       int tiled) {
+                                                       uint8_t* __restrict__ packed, int out_row_bytes,
+                                                       uint8_t* __restrict__ scales, int scale_cols, int tiled) {
     const int lane = threadIdx.x & 31;
     const int group = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     const int row = blockIdx.y;
@@ -116,6 +116,7 @@ __global__ void __launch_bounds__(256) quantize_kernel(const float* __restrict__
         x[c] = col < cols ? __ldcs(reinterpret_cast<const float4*>(src + col)) : make_float4(0.f, 0.f, 0.f, 0.f);
     }
     const int row_bytes = cols / 4 * 3;
+    uint8_t* dst = packed + (size_t)row * out_row_bytes;
 #pragma unroll
     for (int c = 0; c < CHUNKS; c++) {
         const int chunk = chunk0 + c;
@@ -124,35 +125,77 @@ __global__ void __launch_bounds__(256) quantize_kernel(const float* __restrict__
         const uint32_t word = quantize_chunk(x[c], lane, code);
         const int valid = min(96, row_bytes - chunk * 96);  // a multiple of 24 (cols % 32 == 0)
         if (lane < 24 && 4 * lane < valid)
-            *reinterpret_cast<uint32_t*>(packed + (size_t)row * row_bytes + chunk * 96 + 4 * lane) = word;
+            *reinterpret_cast<uint32_t*>(dst + chunk * 96 + 4 * lane) = word;
         const int col = chunk * 128 + 4 * lane;
         if (col < cols && (lane & 7) == 0) {
             const int j = col / 32;  // block index in the row
             size_t off;
             if (tiled) {
-                const size_t atom = (size_t)(row / 128) * (size_t)(cols / 128) + (size_t)(j / 4);
+                const size_t atom = (size_t)(row / 128) * (size_t)(scale_cols / 4) + (size_t)(j / 4);
                 off = atom * 512 + (size_t)((row % 32) * 16 + ((row % 128) / 32) * 4 + (j % 4));
             } else {
-                off = (size_t)row * (cols / 32) + j;
+                off = (size_t)row * scale_cols + j;
             }
             scales[off] = (uint8_t)code;
         }
     }
 }
 
+// Padded rows: zero bytes [row_bytes, out_row_bytes) of each row, and give the scale blocks past
+// the data the finite code 127 (a zero K-tail then contributes 0, never NaN).
+__global__ void pad_tail_kernel(int rows, int row_bytes, uint8_t* __restrict__ packed, int out_row_bytes,
+                                uint8_t* __restrict__ scales, int data_blocks, int scale_cols, int tiled) {
+    const int row = blockIdx.x;
+    if (row >= rows) return;
+    uint8_t* dst = packed + (size_t)row * out_row_bytes;
+    for (int i = row_bytes + threadIdx.x; i < out_row_bytes; i += blockDim.x) dst[i] = 0;
+    for (int j = data_blocks + threadIdx.x; j < scale_cols; j += blockDim.x) {
+        size_t off;
+        if (tiled) {
+            const size_t atom = (size_t)(row / 128) * (size_t)(scale_cols / 4) + (size_t)(j / 4);
+            off = atom * 512 + (size_t)((row % 32) * 16 + ((row % 128) / 32) * 4 + (j % 4));
+        } else {
+            off = (size_t)row * scale_cols + j;
+        }
+        scales[off] = 127;
+    }
+}
+
+// Copy rows between strides, zero-filling each destination row past bytes_used (re-padding
+// compact operand rows for the tensor-memory accelerator). One block per row, 16-byte stores
+// when both strides allow, else bytes.
+__global__ void repad_kernel(const uint8_t* __restrict__ src, int rows, int src_row_bytes, int bytes_used,
+                             uint8_t* __restrict__ dst, int dst_row_bytes) {
+    const int row = blockIdx.x;
+    if (row >= rows) return;
+    const uint8_t* s = src + (size_t)row * src_row_bytes;
+    uint8_t* d = dst + (size_t)row * dst_row_bytes;
+    const bool vec = ((reinterpret_cast<uintptr_t>(s) | reinterpret_cast<uintptr_t>(d)) & 15) == 0;
+    int i = 0;
+    if (vec) {
+        for (i = 16 * threadIdx.x; i + 16 <= bytes_used; i += 16 * blockDim.x)
+            *reinterpret_cast<uint4*>(d + i) = *reinterpret_cast<const uint4*>(s + i);
+        i = bytes_used / 16 * 16;
+    }
+    for (int j = i + threadIdx.x; j < bytes_used; j += blockDim.x) d[j] = s[j];
+    for (int j = bytes_used + threadIdx.x; j < dst_row_bytes; j += blockDim.x) d[j] = 0;
+}
+
 }  // namespace
 }  // namespace mxfp6
 
-extern "C" int mxfp6_quantize_device(const float* d_mat, int rows, int cols, uint8_t* d_packed, uint8_t* d_scales,
-                                     int scale_layout, void* stream) {
+extern "C" int mxfp6_quantize_device_padded(const float* d_mat, int rows, int cols, int padded_cols, uint8_t* d_packed,
+                                            uint8_t* d_scales, int scale_layout, void* stream) {
     using namespace mxfp6;
-    if (!d_mat || !d_packed || !d_scales || rows <= 0 || cols <= 0 || cols % 32 ||
-        (scale_layout != 0 && scale_layout != 1) || (scale_layout == 1 && cols % 128)) {
-        std::fprintf(stderr, "[mxfp6] quantize_device: invalid arguments (%d x %d, layout %d)\n", rows, cols,
-                     scale_layout);
+    if (!d_mat || !d_packed || !d_scales || rows <= 0 || cols <= 0 || cols % 32 || padded_cols < cols ||
+        padded_cols % 32 || (scale_layout != 0 && scale_layout != 1) || (scale_layout == 1 && padded_cols % 128)) {
+        std::fprintf(stderr, "[mxfp6] quantize_device: invalid arguments (%d x %d padded to %d, layout %d)\n", rows,
+                     cols, padded_cols, scale_layout);
         return MXFP6_ERR_INVALID_SHAPE;
     }
-    if ((reinterpret_cast<uintptr_t>(d_mat) & 15) || (reinterpret_cast<uintptr_t>(d_packed) & 3)) {
+    const int out_row_bytes = padded_cols / 4 * 3;
+    if ((reinterpret_cast<uintptr_t>(d_mat) & 15) || (reinterpret_cast<uintptr_t>(d_packed) & 3) || (cols % 4) ||
+        (out_row_bytes % 4)) {
         std::fprintf(stderr, "[mxfp6] quantize_device: input must be 16-byte and output 4-byte aligned\n");
         return MXFP6_ERR_MISALIGNED;
     }
@@ -160,14 +203,46 @@ extern "C" int mxfp6_quantize_device(const float* d_mat, int rows, int cols, uin
         std::fprintf(stderr, "[mxfp6] quantize_device: at most 65535 rows per call\n");
         return MXFP6_ERR_INVALID_SHAPE;
     }
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
     const int chunks = (cols + 127) / 128;
     const int groups = (chunks + CHUNKS - 1) / CHUNKS;
     dim3 grid((groups + 7) / 8, rows);
-    quantize_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(d_mat, rows, cols, d_packed, d_scales,
-                                                                        scale_layout);
+    quantize_kernel<<<grid, 256, 0, st>>>(d_mat, rows, cols, d_packed, out_row_bytes, d_scales, padded_cols / 32,
+                                          scale_layout);
     cudaError_t e = cudaGetLastError();
+    if (e == cudaSuccess && padded_cols > cols) {
+        pad_tail_kernel<<<rows, 128, 0, st>>>(rows, cols / 4 * 3, d_packed, out_row_bytes, d_scales, cols / 32,
+                                             padded_cols / 32, scale_layout);
+        e = cudaGetLastError();
+        if (e == cudaSuccess) note_launch();
+    }
     if (e != cudaSuccess) {
         std::fprintf(stderr, "[mxfp6] quantize_device launch failed: %s\n", cudaGetErrorString(e));
+        return MXFP6_ERR_CUDA;
+    }
+    note_launch();
+    return MXFP6_OK;
+}
+
+extern "C" int mxfp6_quantize_device(const float* d_mat, int rows, int cols, uint8_t* d_packed, uint8_t* d_scales,
+                                     int scale_layout, void* stream) {
+    return mxfp6_quantize_device_padded(d_mat, rows, cols, cols, d_packed, d_scales, scale_layout, stream);
+}
+
+extern "C" int mxfp6_repad_rows_device(const void* d_src, int rows, int src_row_bytes, int bytes_used, void* d_dst,
+                                       int dst_row_bytes, void* stream) {
+    using namespace mxfp6;
+    if (!d_src || !d_dst || rows <= 0 || bytes_used <= 0 || bytes_used > src_row_bytes ||
+        bytes_used > dst_row_bytes) {
+        std::fprintf(stderr, "[mxfp6] repad_rows_device: invalid arguments\n");
+        return MXFP6_ERR_INVALID_STRIDE;
+    }
+    repad_kernel<<<rows, 128, 0, static_cast<cudaStream_t>(stream)>>>(static_cast<const uint8_t*>(d_src), rows,
+                                                                     src_row_bytes, bytes_used,
+                                                                     static_cast<uint8_t*>(d_dst), dst_row_bytes);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) {
+        std::fprintf(stderr, "[mxfp6] repad_rows_device launch failed: %s\n", cudaGetErrorString(e));
         return MXFP6_ERR_CUDA;
     }
     note_launch();

@@ -77,6 +77,38 @@ __device__ __forceinline__ bool wait_parity_bounded(uint32_t bar, uint32_t parit
     }
 }
 
+// Spin for about `ns` nanoseconds (bounded settle time on abort paths).
+__device__ __forceinline__ void settle_ns(unsigned long long ns) {
+    unsigned long long t0, t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+    do {
+        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    } while (t - t0 < ns);
+}
+
+// ---- cp.async (non-bulk) ------------------------------------------------------------------------
+// 4-byte asynchronous global -> shared copies for operands the tensor-memory accelerator cannot
+// address. src_bytes < 4 zero-fills the rest of the word (0 reads nothing). Completion is
+// signalled to an mbarrier with cp_async_mbar_arrive_noinc; the consumer waits on that barrier
+// before tcgen05.mma reads the data.
+__device__ __forceinline__ void cp_async_4(uint32_t dst, const void* src, uint32_t src_bytes) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
+}
+
+__device__ __forceinline__ void cp_async_commit() {
+    asm volatile("cp.async.commit_group;" ::: "memory");
+}
+
+__device__ __forceinline__ void cp_async_wait_all() {
+    asm volatile("cp.async.wait_all;" ::: "memory");
+}
+
+// Arrive on a local mbarrier once every cp.async this thread issued so far has landed; counts as
+// one of the barrier's expected arrivals (.noinc). The thread does not wait.
+__device__ __forceinline__ void cp_async_mbar_arrive_noinc(uint32_t bar) {
+    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(bar) : "memory");
+}
+
 // ---- TMA ---------------------------------------------------------------------------------------
 
 __device__ __forceinline__ void prefetch_tmap(const void* tmap) {

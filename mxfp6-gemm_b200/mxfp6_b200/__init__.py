@@ -64,6 +64,10 @@ launch_count = _fn("mxfp6_launch_count", C.c_uint64, [])
 _quantize = _fn("mxfp6_quantize", None, [_f32p, C.c_int, C.c_int, _u8p, _u8p, C.c_int])
 _quantize_dev = _fn("mxfp6_quantize_device", C.c_int,
                     [C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_int, C.c_void_p])
+_quantize_dev_p = _fn("mxfp6_quantize_device_padded", C.c_int,
+                      [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_int, C.c_void_p])
+_repad_dev = _fn("mxfp6_repad_rows_device", C.c_int,
+                 [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_int, C.c_void_p])
 _dequantize = _fn("mxfp6_dequantize", None, [_u8p, _u8p, C.c_int, C.c_int, _f32p])
 _tiled_bytes = _fn("mxfp6_tiled_scale_bytes", C.c_size_t, [C.c_int, C.c_int])
 _tile = _fn("mxfp6_tile_scales", None, [_u8p, C.c_int, C.c_int, _u8p])
@@ -90,6 +94,18 @@ K_TILE = _k_tile()
 
 def kpad(K: int) -> int:
     return _kpad(K)
+
+
+def a_compact_end_pad(K: int) -> int:
+    """Spare bytes the reference asks for after a compact A buffer (never read here)."""
+    return kpad(K) * 3 // 4 - K * 3 // 4
+
+
+def pad_scales_k(scales: np.ndarray, dim: int, K: int) -> np.ndarray:
+    """Raw scales [dim][K/32] -> [dim][kpad(K)/32], tail blocks code 127 (finite, 2^0)."""
+    out = np.full((dim, kpad(K) // 32), 127, np.uint8)
+    out[:, :K // 32] = np.asarray(scales, np.uint8).reshape(dim, K // 32)
+    return out
 
 
 @dataclass(frozen=True)
@@ -192,6 +208,17 @@ def quantize_device(d_mat, rows, cols, d_packed, d_scales, tiled=False, stream=N
     """quantize_to_mxfp6 on the GPU (device pointers); scales raw or in the GEMM's atom layout."""
     s = 0 if stream is None else (stream.cuda_stream if hasattr(stream, "cuda_stream") else _addr(stream))
     return _quantize_dev(_addr(d_mat), rows, cols, _addr(d_packed), _addr(d_scales), 1 if tiled else 0, s)
+
+
+def quantize_device_padded(d_mat, rows, cols, padded_cols, d_packed, d_scales, tiled=False, stream=None) -> int:
+    s = 0 if stream is None else (stream.cuda_stream if hasattr(stream, "cuda_stream") else _addr(stream))
+    return _quantize_dev_p(_addr(d_mat), rows, cols, padded_cols, _addr(d_packed), _addr(d_scales),
+                           1 if tiled else 0, s)
+
+
+def repad_rows_device(d_src, rows, src_row_bytes, bytes_used, d_dst, dst_row_bytes, stream=None) -> int:
+    s = 0 if stream is None else (stream.cuda_stream if hasattr(stream, "cuda_stream") else _addr(stream))
+    return _repad_dev(_addr(d_src), rows, src_row_bytes, bytes_used, _addr(d_dst), dst_row_bytes, s)
 
 
 def dequantize_mxfp6(q: QuantizedMatrix) -> np.ndarray:

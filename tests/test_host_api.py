@@ -156,7 +156,9 @@ def test_workspace_query_on_degenerate_shapes(lib):
     (dict(Br=112), "ERR_INVALID_STRIDE"),
     (dict(dA=0), "ERR_NULL_POINTER"),
     (dict(dD=0), "ERR_NULL_POINTER"),
-    (dict(dA=0x1010), "ERR_MISALIGNED"),
+    (dict(dA=0x1002), "ERR_MISALIGNED"),
+    (dict(Kp=256, Ar=96, Br=192), "ERR_INVALID_STRIDE"),   # compact stride of K=128 < kpad^-1(256)
+    (dict(Kp=256, Ar=190, Br=192), "ERR_INVALID_STRIDE"),  # not a multiple of 4
     (dict(dsB=0x1008), "ERR_MISALIGNED"),
     (dict(ot=7), "ERR_INVALID_OUT_TYPE"),
 ])

@@ -87,3 +87,29 @@ def test_every_golden_encode_input(lib, golden):
     codes = lib.unpack_codes(p).reshape(-1, 32)[:nblk, 1:].reshape(-1)[:len(xs)]
     bad = np.nonzero(codes != want)[0]
     assert bad.size == 0, f"{bad.size} mismatches, first inputs {xs[bad[:5]]}"
+
+
+@pytest.mark.parametrize("tiled", [False, True])
+@pytest.mark.parametrize("rows,cols", [(128, 224), (256, 3808), (130, 160)])
+def test_padded_output_rows(lib, rows, cols, tiled):
+    """quantize_device_padded: rows of kpad(cols) codes with a zero tail, scales extended with
+    code 127 (pad_scales_k), the first cols codes identical to the host quantiser."""
+    if tiled and rows % 128:
+        pytest.skip("tiled scales cover whole 128-row blocks")
+    m = _special_matrix(rows, cols, 3 * rows + cols)
+    host = lib.quantize_to_mxfp6(m)
+    Kp = lib.kpad(cols)
+    d = torch.from_numpy(m).cuda()
+    packed = torch.full((rows, Kp * 3 // 4), 0xA5, dtype=torch.uint8, device="cuda")
+    nsc = lib.tiled_scale_bytes(rows, Kp) if tiled else rows * Kp // 32
+    scales = torch.full((nsc,), 0xA5, dtype=torch.uint8, device="cuda")
+    assert lib.quantize_device_padded(d, rows, cols, Kp, packed, scales, tiled) == lib.OK
+    torch.cuda.synchronize()
+    p, s = packed.cpu().numpy(), scales.cpu().numpy()
+    assert np.array_equal(p[:, :cols * 3 // 4], host.packed_data)
+    assert not p[:, cols * 3 // 4:].any()
+    want = lib.pad_scales_k(host.scales, rows, cols)
+    if tiled:
+        assert np.array_equal(s, lib.preprocess_scale(want, rows, Kp))
+    else:
+        assert np.array_equal(s.reshape(rows, Kp // 32), want)
