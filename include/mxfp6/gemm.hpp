@@ -48,8 +48,11 @@ size_t gemm_workspace_size(int M, int N, int Kp);
 
 // D[M,N] = A[M,K] * B[K,N]; see the layout notes above. Requirements (checked; a violation
 // prints "[mxfp6] ..." to stderr, records an error for mxfp6_last_error() and launches nothing):
-//   M % 128 == 0, N % 128 == 0, Kp % 128 == 0, Kp > 0, A_row_bytes and B_row_bytes >= 0.75*Kp
-//   and multiples of 32, dA/dBsh 32-byte aligned, dsA/dsB/dD 16-byte aligned.
+//   M % 128 == 0, N % 128 == 0, Kp % 128 == 0, Kp > 0; B_row_bytes >= 0.75*Kp and a multiple of
+//   32, dBsh 32-byte aligned; A_row_bytes a multiple of 4 holding the row's K codes
+//   (> 0.75*Kp - 96: the reference's compact stride 3K/4 qualifies), dA 4-byte aligned (A strides
+//   that are multiples of 32 on a 32-byte aligned base take the tensor load, others the kernels'
+//   loader warps); dsA/dsB/dD 16-byte aligned.
 // If the shape would split but ws is null or smaller than gemm_workspace_size(), gemm() runs
 // unsplit (still correct) and warns on stderr, as the reference does.
 void gemm(OutType ot, int M, int N, int Kp, const void* dA, const void* dBsh, const uint8_t* dsA,

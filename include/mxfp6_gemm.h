@@ -36,8 +36,11 @@ enum mxfp6_out_type { MXFP6_OUT_F32 = 0, MXFP6_OUT_F16 = 1, MXFP6_OUT_BF16 = 2 }
 enum mxfp6_status {
     MXFP6_OK = 0,
     MXFP6_ERR_INVALID_SHAPE = 1,     /* M, N or Kp not a positive multiple of 128 */
-    MXFP6_ERR_INVALID_STRIDE = 2,    /* row bytes < 0.75*Kp or not a multiple of 32 */
-    MXFP6_ERR_MISALIGNED = 3,        /* a pointer violates its alignment rule */
+    MXFP6_ERR_INVALID_STRIDE = 2,    /* B row bytes < 0.75*Kp or not a multiple of 32; A row bytes
+                                        not a multiple of 4 or <= 0.75*Kp - 96 (shorter than any
+                                        K with kpad(K) == Kp) */
+    MXFP6_ERR_MISALIGNED = 3,        /* a pointer violates its alignment rule (A 4, B 32, scales and
+                                        D 16 bytes) */
     MXFP6_ERR_NULL_POINTER = 4,      /* a required pointer is null */
     MXFP6_ERR_INVALID_OUT_TYPE = 5,  /* ot not one of mxfp6_out_type */
     MXFP6_ERR_CUDA = 6,              /* a CUDA runtime / driver call failed */
@@ -54,7 +57,10 @@ enum mxfp6_status {
 
 /* D[M,N] = A[M,K]·B[K,N] on the legacy default stream. ot: mxfp6_out_type. See
  * include/mxfp6/gemm.hpp for layouts and requirements. On a validation error nothing is
- * launched, a message goes to stderr and mxfp6_last_error() returns the code. */
+ * launched, a message goes to stderr and mxfp6_last_error() returns the code.
+ * A_row_bytes may be the reference's compact stride 3K/4 (K % 128 != 0, scales extended with
+ * pad_scales_k): such an A, or any A whose stride is not a multiple of 32 bytes or whose base is
+ * not 32-byte aligned, is loaded by the kernels' loader warps instead of the tensor load. */
 void mxfp6_gemm(int ot, int M, int N, int Kp, const void* dA, const void* dBsh, const uint8_t* dsA,
                 const uint8_t* dsB, void* dD, int A_row_bytes, int B_row_bytes, void* ws,
                 size_t ws_bytes);
