@@ -42,27 +42,30 @@ __device__ __forceinline__ uint32_t ceil_pow2_code(float v) {
     return (uint32_t)(code < 0 ? 0 : (code > 254 ? 254 : code));
 }
 
-// Nearest E2M3 code, ties to even, saturating at 7.5, from the float's bits. Below 1.0 the grid
-// is 1/8 (an exact *8 and round-half-even); from 1.0 to 7.5 the 23-bit mantissa is rounded to 3
-// bits, and a mantissa carry moves into the exponent field by plain addition. Same results as
-// the reference's conversion (include/mxfp6/types.hpp:26-72), NaN -> 0x18 included.
-__device__ __forceinline__ uint32_t to_e2m3(float v) {
-    const uint32_t b = __float_as_uint(v);
-    const uint32_t a = b & 0x7FFFFFFFu;
-    if (a > 0x7F800000u) return 0x18;                  // NaN
-    const uint32_t sgn = v < 0.0f ? 0x20u : 0u;        // -0.0 keeps code 0
-    uint32_t code;
-    if (a >= 0x40F00000u) {                            // >= 7.5 (Inf included): saturate
-        code = 0x1F;
-    } else if (a < 0x3F800000u) {                      // < 1.0: subnormal grid of 1/8
-        code = (uint32_t)__float2int_rn(__uint_as_float(a) * 8.0f);  // 0..8; 8 is the code of 1.0
-    } else {
-        const uint32_t ex = (a >> 23) - 127u;          // 0, 1 or 2
-        const uint32_t man = a & 0x7FFFFFu;
-        const uint32_t m3 = (man + 0x7FFFFu + ((man >> 20) & 1u)) >> 20;  // 0..8
-        code = ((ex + 1u) << 3) + m3;
-    }
-    return sgn | code;
+// E8M0 code of the reference's block scale for block max m >= 0: the smallest power of two
+// >= RN(m / 7.5), 127 for m == 0. For P = 2^e >= 2^-125, RN(m / 7.5) <= P exactly when
+// m <= 7.5 * P (the rounding boundary P + ulp(P)/2 lies below the next float above 7.5 * P), so
+// with m = 1.f * 2^E the code is E - 2, plus 1 when the mantissa exceeds 1.875, plus the bias.
+// Subnormal quotients, an infinite max and m == 0 take the division.
+__device__ __forceinline__ uint32_t scale_code(float m) {
+    const uint32_t mb = __float_as_uint(m);
+    const int e = (int)(mb >> 23) - 129 + ((mb & 0x7FFFFFu) > 0x700000u ? 1 : 0);
+    if (mb < 0x7F800000u && (mb >> 23) != 0u && e >= -125) return (uint32_t)(e + 127);
+    return m == 0.0f ? 127u : ceil_pow2_code(__fdiv_rn(m, 7.5f));
+}
+
+// Nearest E2M3 codes of two values (round to nearest even, saturating at 7.5) with the
+// hardware conversion cvt.rn.satfinite.e2m3x2.f32, which writes a's code to the upper byte and
+// b's to the lower one. Two inputs are first replaced so that the codes equal the reference's
+// conversion (include/mxfp6/types.hpp:26-72): NaN -> 4.0 (code 0x18, what the reference yields on
+// x86-64) and -0.0 -> +0.0 (code 0; other negatives that round to zero keep the sign, 0x20).
+// Returns code(b) | code(a) << 8.
+__device__ __forceinline__ uint32_t to_e2m3x2(float a, float b) {
+    a = a != a ? 4.0f : a + 0.0f;
+    b = b != b ? 4.0f : b + 0.0f;
+    uint16_t d;
+    asm("cvt.rn.satfinite.e2m3x2.f32 %0, %1, %2;" : "=h"(d) : "f"(a), "f"(b));
+    return d;
 }
 
 // 1 / 2^(code - 127) = 2^(127 - code), exact for every code the quantiser produces (0..254):
@@ -83,11 +86,12 @@ __device__ __forceinline__ uint32_t quantize_chunk(float4 x, int lane, uint32_t&
         const float o = __shfl_xor_sync(0xffffffffu, m, off);
         if (o > m) m = o;
     }
-    code = m == 0.0f ? 127u : ceil_pow2_code(__fdiv_rn(m, 7.5f));
+    code = scale_code(m);
     const float inv = e8m0_reciprocal(code);
-    const uint32_t q0 = to_e2m3(x.x * inv), q1 = to_e2m3(x.y * inv), q2 = to_e2m3(x.z * inv),
-                   q3 = to_e2m3(x.w * inv);
-    const uint32_t g = q0 | (q1 << 6) | (q2 << 12) | (q3 << 18);  // this lane's 3 bytes
+    const uint32_t p01 = to_e2m3x2(x.y * inv, x.x * inv);  // code(x) | code(y) << 8
+    const uint32_t p23 = to_e2m3x2(x.w * inv, x.z * inv);
+    const uint32_t g = (p01 & 0x3Fu) | ((p01 >> 2) & 0xFC0u) | ((p23 & 0x3Fu) << 12) | ((p23 >> 2) & 0xFC0u) << 12;
+    // g: this lane's 3 bytes, codes x, y, z, w at bits 0, 6, 12, 18
     // Bytes [3*lane, 3*lane + 3) of the chunk's 96; lane w < 24 packs word w = bytes [4w, 4w + 4).
     const int lo = (4 * lane) / 3;
     const uint32_t glo = __shfl_sync(0xffffffffu, g, lo & 31);
