@@ -15,6 +15,7 @@
  *   mxfp6_last_error      status of the last call on this thread (0 = ok).
  *   mxfp6_device_status   synchronises the device and returns/clears the kernel status word
  *                         (bounded waits inside the kernel record timeouts there).
+ *   mxfp6_gemm_gather     the GEMM with its output written to several (peer) destinations.
  *
  * Host preprocessing helpers (the C face of mxfp6/preprocess.hpp, used by bindings that cannot
  * instantiate the C++ header) are declared at the end.
@@ -78,6 +79,25 @@ size_t mxfp6_gemm_workspace_size(int M, int N, int Kp);
 /* The same for one output type (no counterpart in the reference): a caller that knows ot can
  * allocate exactly what that call uses. */
 size_t mxfp6_gemm_workspace_size_out(int ot, int M, int N, int Kp);
+
+/* Column-parallel GEMM whose epilogue also performs the all-gather of the shards (no
+ * counterpart in the reference, whose multi-GPU use is left to the caller): D = A·B (this
+ * rank's N columns) is written into each of the n_dst (1..8) row-major [M][ldd] matrices dDs[i]
+ * at column col0 — typically this rank's gathered output and its peers' (pointers from
+ * mxfp6_ipc_import, reached over NVLink with plain peer stores). ldd and col0 must keep 16-byte
+ * aligned rows. The kernel never waits on a peer: the caller orders the ranks (synchronise the
+ * stream, then a barrier) before reading the gathered output. Same validation and workspace
+ * contract as mxfp6_gemm_stream. */
+void mxfp6_gemm_gather(int ot, int M, int N, int Kp, const void* dA, const void* dBsh, const uint8_t* dsA,
+                       const uint8_t* dsB, void* const* dDs, int n_dst, long long ldd, int col0, int A_row_bytes,
+                       int B_row_bytes, void* ws, size_t ws_bytes, void* stream);
+
+/* CUDA IPC for mxfp6_gemm_gather's peer destinations. export: a 64-byte handle of the
+ * allocation holding dptr, and dptr's offset in it. import (in another process, with its own
+ * device current): maps the allocation, returns its base (for close) and the pointer. */
+int mxfp6_ipc_export(const void* dptr, void* handle_out, size_t* offset_out);
+int mxfp6_ipc_import(const void* handle, size_t offset, void** base_out, void** dptr_out);
+int mxfp6_ipc_close(void* base);
 
 /* Route for (M,N,Kp): writes MT, NT, MPW, NPW into out[0..3]. */
 void mxfp6_choose_tile(int M, int N, int Kp, int* out4);

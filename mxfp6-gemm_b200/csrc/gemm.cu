@@ -133,6 +133,24 @@ bool a_uses_tma(int Kp, const void* dA, int A_row_bytes) {
     return A_row_bytes % 32 == 0 && (long long)A_row_bytes >= (long long)Kp * 3 / 4 && aligned(dA, 32);
 }
 
+// One destination: the plain GEMM's row-major [M][N] D.
+kern::DstList single_dst(void* dD, int N) {
+    kern::DstList dl{};
+    dl.p[0] = dD;
+    dl.n = 1;
+    dl.col0 = 0;
+    dl.ldd = N;
+    return dl;
+}
+
+// 256-bit stores need every destination row chunk 32-byte aligned.
+bool dst_align32(const kern::DstList& dl, size_t esize) {
+    if ((dl.ldd * (long long)esize) % 32 || ((long long)dl.col0 * (long long)esize) % 32) return false;
+    for (int d = 0; d < dl.n; d++)
+        if (!aligned(dl.p[d], 32)) return false;
+    return true;
+}
+
 // Producer for A: the 16U6 tensor load, or the loader warps' 4-byte cp.async copies.
 int a_mode(int Kp, const void* dA, int A_row_bytes) {
     return a_uses_tma(Kp, dA, A_row_bytes) ? kern::A_TMA : kern::A_CPASYNC;
@@ -199,8 +217,8 @@ bool make_a_tmap(int amode, CUtensorMap* map, const void* dA, int M, int Kp, int
 
 template <int BN, typename OutT, bool PARTIAL, int AMODE>
 bool launch_gemm(int M, int N, int Kp, const void* dA, const void* dB, const uint8_t* sA,
-                 const uint8_t* sB, void* dD, float* ws, int A_row_bytes, int B_row_bytes, int splits,
-                 cudaStream_t stream) {
+                 const uint8_t* sB, const kern::DstList& dl, float* ws, int A_row_bytes, int B_row_bytes,
+                 int splits, cudaStream_t stream) {
     using C = kern::Config<BN, AMODE>;
     auto kernel = kern::gemm_mxfp6_sm100<BN, OutT, PARTIAL, AMODE>;
     static std::once_flag attr_once[kMaxDevices];
@@ -226,7 +244,7 @@ bool launch_gemm(int M, int N, int Kp, const void* dA, const void* dB, const uin
     kern::Params p;
     p.sfA = sA;
     p.sfB = sB;
-    p.D = dD;
+    p.dst = dl;
     p.ws = ws;
     p.M = M;
     p.N = N;
@@ -235,7 +253,7 @@ bool launch_gemm(int M, int N, int Kp, const void* dA, const void* dB, const uin
     p.n_blocks = (N + BN - 1) / BN;
     p.k_slabs = Kp / kern::BK;
     p.splits = splits;
-    p.out_align32 = aligned(PARTIAL ? static_cast<const void*>(ws) : dD, 32) ? 1 : 0;
+    p.out_align32 = (PARTIAL ? aligned(ws, 32) : dst_align32(dl, sizeof(OutT))) ? 1 : 0;
     set_compact(p, Kp, dA, A_row_bytes);
     const long long tiles = (long long)p.m_blocks * p.n_blocks * splits;
     const int grid = (int)(tiles < sm_count() ? tiles : sm_count());
@@ -251,7 +269,8 @@ bool launch_gemm(int M, int N, int Kp, const void* dA, const void* dB, const uin
 
 template <typename OutT, bool PARTIAL, int AMODE>
 bool launch_pair(int M, int N, int Kp, const void* dA, const void* dB, const uint8_t* sA, const uint8_t* sB,
-                 void* dD, float* ws, int A_row_bytes, int B_row_bytes, int splits, cudaStream_t stream) {
+                 const kern::DstList& dl, float* ws, int A_row_bytes, int B_row_bytes, int splits,
+                 cudaStream_t stream) {
     using C = kern::PairConfig<AMODE>;
     auto kernel = kern::gemm_mxfp6_sm100_pair<OutT, PARTIAL, AMODE>;
     static std::once_flag attr_once[kMaxDevices];
@@ -277,7 +296,7 @@ bool launch_pair(int M, int N, int Kp, const void* dA, const void* dB, const uin
     kern::Params p;
     p.sfA = sA;
     p.sfB = sB;
-    p.D = dD;
+    p.dst = dl;
     p.ws = ws;
     p.M = M;
     p.N = N;
@@ -286,7 +305,7 @@ bool launch_pair(int M, int N, int Kp, const void* dA, const void* dB, const uin
     p.n_blocks = (N + C::BN - 1) / C::BN;
     p.k_slabs = Kp / kern::BK;
     p.splits = splits;
-    p.out_align32 = aligned(PARTIAL ? static_cast<const void*>(ws) : dD, 32) ? 1 : 0;
+    p.out_align32 = (PARTIAL ? aligned(ws, 32) : dst_align32(dl, sizeof(OutT))) ? 1 : 0;
     set_compact(p, Kp, dA, A_row_bytes);
     const long long units = (long long)p.m_blocks * p.n_blocks * splits;
     const int pairs = sm_count() / 2;
@@ -314,13 +333,13 @@ bool launch_pair(int M, int N, int Kp, const void* dA, const void* dB, const uin
 }
 
 template <typename OutT>
-bool launch_reduce(const float* ws, void* dD, int M, int N, int splits, cudaStream_t stream) {
+bool launch_reduce(const float* ws, const kern::DstList& dl, int M, int N, int splits, cudaStream_t stream) {
     const long long total = (long long)M * N;
     const long long n4 = total / 4;
     long long blocks = (n4 + 255) / 256;
     const long long cap = (long long)sm_count() * 8;
     if (blocks > cap) blocks = cap;
-    kern::reduce_partials<OutT><<<(int)blocks, 256, 0, stream>>>(ws, static_cast<OutT*>(dD), total, splits);
+    kern::reduce_partials<OutT><<<(int)blocks, 256, 0, stream>>>(ws, dl, N, total, splits);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) {
         set_error(MXFP6_ERR_CUDA, "split-K reduce launch failed: %s", cudaGetErrorString(e));
@@ -334,42 +353,42 @@ bool launch_reduce(const float* ws, void* dD, int M, int N, int splits, cudaStre
 // instantiation; the reduce pass converts.
 template <typename OutT, int AMODE>
 bool run_route(const Route& r, int M, int N, int Kp, const void* dA, const void* dB, const uint8_t* sA,
-               const uint8_t* sB, void* dD, int Ar, int Br, void* ws, cudaStream_t stream) {
+               const uint8_t* sB, const kern::DstList& dl, int Ar, int Br, void* ws, cudaStream_t stream) {
     float* wsf = static_cast<float*>(ws);
     const bool part = r.splits > 1;
     bool ok;
     if (r.MT == 256) {
-        ok = part ? launch_pair<float, true, AMODE>(M, N, Kp, dA, dB, sA, sB, dD, wsf, Ar, Br, r.splits, stream)
-                  : launch_pair<OutT, false, AMODE>(M, N, Kp, dA, dB, sA, sB, dD, wsf, Ar, Br, 1, stream);
+        ok = part ? launch_pair<float, true, AMODE>(M, N, Kp, dA, dB, sA, sB, dl, wsf, Ar, Br, r.splits, stream)
+                  : launch_pair<OutT, false, AMODE>(M, N, Kp, dA, dB, sA, sB, dl, wsf, Ar, Br, 1, stream);
     } else if (r.NT == 256) {
-        ok = part ? launch_gemm<256, float, true, AMODE>(M, N, Kp, dA, dB, sA, sB, dD, wsf, Ar, Br, r.splits,
+        ok = part ? launch_gemm<256, float, true, AMODE>(M, N, Kp, dA, dB, sA, sB, dl, wsf, Ar, Br, r.splits,
                                                            stream)
-                  : launch_gemm<256, OutT, false, AMODE>(M, N, Kp, dA, dB, sA, sB, dD, wsf, Ar, Br, 1, stream);
+                  : launch_gemm<256, OutT, false, AMODE>(M, N, Kp, dA, dB, sA, sB, dl, wsf, Ar, Br, 1, stream);
     } else {
-        ok = part ? launch_gemm<128, float, true, AMODE>(M, N, Kp, dA, dB, sA, sB, dD, wsf, Ar, Br, r.splits,
+        ok = part ? launch_gemm<128, float, true, AMODE>(M, N, Kp, dA, dB, sA, sB, dl, wsf, Ar, Br, r.splits,
                                                            stream)
-                  : launch_gemm<128, OutT, false, AMODE>(M, N, Kp, dA, dB, sA, sB, dD, wsf, Ar, Br, 1, stream);
+                  : launch_gemm<128, OutT, false, AMODE>(M, N, Kp, dA, dB, sA, sB, dl, wsf, Ar, Br, 1, stream);
     }
-    return ok && (!part || launch_reduce<OutT>(wsf, dD, M, N, r.splits, stream));
+    return ok && (!part || launch_reduce<OutT>(wsf, dl, M, N, r.splits, stream));
 }
 
 template <typename OutT>
 bool run_typed(const Route& r, int M, int N, int Kp, const void* dA, const void* dB, const uint8_t* sA,
-               const uint8_t* sB, void* dD, int Ar, int Br, void* ws, cudaStream_t stream) {
+               const uint8_t* sB, const kern::DstList& dl, int Ar, int Br, void* ws, cudaStream_t stream) {
     return a_mode(Kp, dA, Ar) == kern::A_TMA
-               ? run_route<OutT, kern::A_TMA>(r, M, N, Kp, dA, dB, sA, sB, dD, Ar, Br, ws, stream)
-               : run_route<OutT, kern::A_CPASYNC>(r, M, N, Kp, dA, dB, sA, sB, dD, Ar, Br, ws, stream);
+               ? run_route<OutT, kern::A_TMA>(r, M, N, Kp, dA, dB, sA, sB, dl, Ar, Br, ws, stream)
+               : run_route<OutT, kern::A_CPASYNC>(r, M, N, Kp, dA, dB, sA, sB, dl, Ar, Br, ws, stream);
 }
 
 bool run(int ot, const Route& r, int M, int N, int Kp, const void* dA, const void* dB, const uint8_t* sA,
-         const uint8_t* sB, void* dD, int Ar, int Br, void* ws, cudaStream_t stream) {
+         const uint8_t* sB, const kern::DstList& dl, int Ar, int Br, void* ws, cudaStream_t stream) {
     switch (ot) {
         case MXFP6_OUT_F32:
-            return run_typed<float>(r, M, N, Kp, dA, dB, sA, sB, dD, Ar, Br, ws, stream);
+            return run_typed<float>(r, M, N, Kp, dA, dB, sA, sB, dl, Ar, Br, ws, stream);
         case MXFP6_OUT_F16:
-            return run_typed<__half>(r, M, N, Kp, dA, dB, sA, sB, dD, Ar, Br, ws, stream);
+            return run_typed<__half>(r, M, N, Kp, dA, dB, sA, sB, dl, Ar, Br, ws, stream);
         default:
-            return run_typed<__nv_bfloat16>(r, M, N, Kp, dA, dB, sA, sB, dD, Ar, Br, ws, stream);
+            return run_typed<__nv_bfloat16>(r, M, N, Kp, dA, dB, sA, sB, dl, Ar, Br, ws, stream);
     }
 }
 
@@ -379,10 +398,10 @@ Route route_for_out(int ot, int M, int N, int Kp) {
 }
 
 void gemm_entry(int ot, int M, int N, int Kp, const void* dA, const void* dB, const uint8_t* sA,
-                const uint8_t* sB, void* dD, int Ar, int Br, void* ws, size_t ws_bytes,
+                const uint8_t* sB, const kern::DstList& dl, int Ar, int Br, void* ws, size_t ws_bytes,
                 cudaStream_t stream) {
     t_last_error = MXFP6_OK;
-    if (!validate(ot, M, N, Kp, dA, dB, sA, sB, dD, Ar, Br)) return;
+    if (!validate(ot, M, N, Kp, dA, dB, sA, sB, dl.p[0], Ar, Br)) return;
     Route r = route_for_out(ot, M, N, Kp);
     if (r.splits > 1) {
         const size_t need = splitk_bytes(M, N, r.splits);
@@ -395,7 +414,7 @@ void gemm_entry(int ot, int M, int N, int Kp, const void* dA, const void* dB, co
             r.splits = 1;
         }
     }
-    run(ot, r, M, N, Kp, dA, dB, sA, sB, dD, Ar, Br, ws, stream);
+    run(ot, r, M, N, Kp, dA, dB, sA, sB, dl, Ar, Br, ws, stream);
 }
 
 // ---- split-K scratch owned by the library (mxfp6_gemm_static_workspace) --------------------------------
@@ -447,7 +466,8 @@ size_t gemm_workspace_size(int M, int N, int Kp) {
 
 void gemm(OutType ot, int M, int N, int Kp, const void* dA, const void* dBsh, const uint8_t* dsA,
           const uint8_t* dsB, void* dD, int A_row_bytes, int B_row_bytes, void* ws, size_t ws_bytes) {
-    gemm_entry((int)ot, M, N, Kp, dA, dBsh, dsA, dsB, dD, A_row_bytes, B_row_bytes, ws, ws_bytes, 0);
+    gemm_entry((int)ot, M, N, Kp, dA, dBsh, dsA, dsB, single_dst(dD, N), A_row_bytes, B_row_bytes, ws, ws_bytes,
+               0);
 }
 
 }  // namespace mxfp6
@@ -461,13 +481,13 @@ extern "C" {
 void mxfp6_gemm(int ot, int M, int N, int Kp, const void* dA, const void* dBsh, const uint8_t* dsA,
                 const uint8_t* dsB, void* dD, int A_row_bytes, int B_row_bytes, void* ws,
                 size_t ws_bytes) {
-    gemm_entry(ot, M, N, Kp, dA, dBsh, dsA, dsB, dD, A_row_bytes, B_row_bytes, ws, ws_bytes, 0);
+    gemm_entry(ot, M, N, Kp, dA, dBsh, dsA, dsB, single_dst(dD, N), A_row_bytes, B_row_bytes, ws, ws_bytes, 0);
 }
 
 void mxfp6_gemm_stream(int ot, int M, int N, int Kp, const void* dA, const void* dBsh,
                        const uint8_t* dsA, const uint8_t* dsB, void* dD, int A_row_bytes,
                        int B_row_bytes, void* ws, size_t ws_bytes, void* stream) {
-    gemm_entry(ot, M, N, Kp, dA, dBsh, dsA, dsB, dD, A_row_bytes, B_row_bytes, ws, ws_bytes,
+    gemm_entry(ot, M, N, Kp, dA, dBsh, dsA, dsB, single_dst(dD, N), A_row_bytes, B_row_bytes, ws, ws_bytes,
                static_cast<cudaStream_t>(stream));
 }
 
@@ -516,7 +536,7 @@ void mxfp6_gemm_force_tile(int ot, int M, int N, int Kp, int MT, int NT, int spl
                   splitk_bytes(M, N, splits), ws_bytes);
         return;
     }
-    run(ot, Route{MT, NT, splits}, M, N, Kp, dA, dBsh, dsA, dsB, dD, A_row_bytes, B_row_bytes, ws,
+    run(ot, Route{MT, NT, splits}, M, N, Kp, dA, dBsh, dsA, dsB, single_dst(dD, N), A_row_bytes, B_row_bytes, ws,
         static_cast<cudaStream_t>(stream));
 }
 
@@ -548,7 +568,76 @@ void mxfp6_gemm_static_workspace(int ot, int M, int N, int Kp, const void* dA, c
             return;
         }
     }
-    run(ot, r, M, N, Kp, dA, dBsh, dsA, dsB, dD, A_row_bytes, B_row_bytes, ws, static_cast<cudaStream_t>(stream));
+    run(ot, r, M, N, Kp, dA, dBsh, dsA, dsB, single_dst(dD, N), A_row_bytes, B_row_bytes, ws,
+        static_cast<cudaStream_t>(stream));
+}
+
+void mxfp6_gemm_gather(int ot, int M, int N, int Kp, const void* dA, const void* dBsh, const uint8_t* dsA,
+                       const uint8_t* dsB, void* const* dDs, int n_dst, long long ldd, int col0, int A_row_bytes,
+                       int B_row_bytes, void* ws, size_t ws_bytes, void* stream) {
+    t_last_error = MXFP6_OK;
+    if (!dDs || n_dst < 1 || n_dst > kern::MAX_DST) {
+        set_error(MXFP6_ERR_NULL_POINTER, "gather: %d destinations (1..%d, non-null list)", n_dst, kern::MAX_DST);
+        return;
+    }
+    const long long esize = ot == MXFP6_OUT_F32 ? 4 : 2;
+    if (col0 < 0 || ldd < (long long)col0 + N || (ldd * esize) % 16 || ((long long)col0 * esize) % 16) {
+        set_error(MXFP6_ERR_INVALID_STRIDE,
+                  "gather: destination pitch %lld and column offset %d must hold N=%d columns and keep "
+                  "16-byte aligned rows",
+                  ldd, col0, N);
+        return;
+    }
+    kern::DstList dl{};
+    for (int d = 0; d < n_dst; d++) {
+        if (!dDs[d] || !aligned(dDs[d], 16)) {
+            set_error(dDs[d] ? MXFP6_ERR_MISALIGNED : MXFP6_ERR_NULL_POINTER,
+                      "gather: destination %d is null or not 16-byte aligned", d);
+            return;
+        }
+        dl.p[d] = dDs[d];
+    }
+    dl.n = n_dst;
+    dl.col0 = col0;
+    dl.ldd = ldd;
+    gemm_entry(ot, M, N, Kp, dA, dBsh, dsA, dsB, dl, A_row_bytes, B_row_bytes, ws, ws_bytes,
+               static_cast<cudaStream_t>(stream));
+}
+
+int mxfp6_ipc_export(const void* dptr, void* handle_out, size_t* offset_out) {
+    using GetRangeFn = CUresult (*)(CUdeviceptr*, size_t*, CUdeviceptr);
+    static GetRangeFn range = [] {
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &f, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            f = nullptr;
+        return reinterpret_cast<GetRangeFn>(f);
+    }();
+    if (!dptr || !handle_out || !offset_out || !range) return MXFP6_ERR_NULL_POINTER;
+    CUdeviceptr base = 0;
+    size_t size = 0;
+    if (range(&base, &size, reinterpret_cast<CUdeviceptr>(dptr)) != CUDA_SUCCESS) return MXFP6_ERR_CUDA;
+    cudaIpcMemHandle_t h;
+    if (cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base)) != cudaSuccess) return MXFP6_ERR_CUDA;
+    std::memcpy(handle_out, &h, sizeof(h));
+    *offset_out = (size_t)(reinterpret_cast<CUdeviceptr>(dptr) - base);
+    return MXFP6_OK;
+}
+
+int mxfp6_ipc_import(const void* handle, size_t offset, void** base_out, void** dptr_out) {
+    if (!handle || !base_out || !dptr_out) return MXFP6_ERR_NULL_POINTER;
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, handle, sizeof(h));
+    void* base = nullptr;
+    if (cudaIpcOpenMemHandle(&base, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) return MXFP6_ERR_CUDA;
+    *base_out = base;
+    *dptr_out = static_cast<uint8_t*>(base) + offset;
+    return MXFP6_OK;
+}
+
+int mxfp6_ipc_close(void* base) {
+    return cudaIpcCloseMemHandle(base) == cudaSuccess ? MXFP6_OK : MXFP6_ERR_CUDA;
 }
 
 size_t mxfp6_static_workspace_bytes(void) {

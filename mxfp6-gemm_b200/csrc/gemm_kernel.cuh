@@ -71,14 +71,25 @@ struct Config {
     static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
 };
 
+// Output destinations: D is written into each of n row-major [M][ldd] matrices at column col0
+// (one destination, ldd = N, col0 = 0 for a plain GEMM; several for a GEMM whose epilogue also
+// delivers its column shard into peers' gathered outputs).
+constexpr int MAX_DST = 8;
+struct DstList {
+    void* p[MAX_DST];
+    int n;
+    int col0;
+    long long ldd;
+};
+
 struct Params {
     const uint8_t* sfA;  // A scales, atom layout
     const uint8_t* sfB;  // B scales, atom layout
-    void* D;             // output (OutT) or nullptr in partial mode
+    DstList dst;         // outputs (OutT); unused in partial mode
     float* ws;           // FP32 partials [splits][M][N] in partial mode
     int M, N, Kp;
     int m_blocks, n_blocks, k_slabs, splits;
-    int out_align32;  // D (or ws in partial mode) is 32-byte aligned: 256-bit stores
+    int out_align32;  // every output row chunk (or ws in partial mode) is 32-byte aligned: 256-bit stores
     // compact A (software producer, compact_a.cuh): packed rows, stride and valid bytes per row
     const uint8_t* a_ptr;
     int a_stride, a_valid;
@@ -131,36 +142,41 @@ __device__ __forceinline__ void store_words(void* dst, const uint32_t* w, bool a
     }
 }
 
+// 32 FP32 accumulator words of one row -> OutT words (RNE): 32 words for float, 16 for half
+// and bfloat16 (two values per word).
 template <typename OutT>
-__device__ __forceinline__ void store_row_chunk(OutT* dst, const uint32_t (&r)[32], bool align32);
+struct ChunkWords {
+    static constexpr int N = std::is_same<OutT, float>::value ? 32 : 16;
+};
 
-template <>
-__device__ __forceinline__ void store_row_chunk<float>(float* dst, const uint32_t (&r)[32], bool align32) {
-    store_words<32>(dst, r, align32);
+template <typename OutT>
+__device__ __forceinline__ void convert_chunk(const uint32_t (&r)[32], uint32_t (&w)[ChunkWords<OutT>::N]) {
+    if constexpr (std::is_same<OutT, float>::value) {
+#pragma unroll
+        for (int i = 0; i < 32; i++) w[i] = r[i];
+    } else if constexpr (std::is_same<OutT, __half>::value) {
+#pragma unroll
+        for (int i = 0; i < 16; i++) {
+            __half2 v = __floats2half2_rn(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1]));
+            w[i] = *reinterpret_cast<uint32_t*>(&v);
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < 16; i++) {
+            __nv_bfloat162 v = __floats2bfloat162_rn(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1]));
+            w[i] = *reinterpret_cast<uint32_t*>(&v);
+        }
+    }
 }
 
-template <>
-__device__ __forceinline__ void store_row_chunk<__half>(__half* dst, const uint32_t (&r)[32], bool align32) {
-    uint32_t h[16];
-#pragma unroll
-    for (int i = 0; i < 16; i++) {
-        __half2 v = __floats2half2_rn(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1]));
-        h[i] = *reinterpret_cast<uint32_t*>(&v);
-    }
-    store_words<16>(dst, h, align32);
-}
-
-template <>
-__device__ __forceinline__ void store_row_chunk<__nv_bfloat16>(__nv_bfloat16* dst, const uint32_t (&r)[32],
-                                                               bool align32) {
-    uint32_t h[16];
-#pragma unroll
-    for (int i = 0; i < 16; i++) {
-        __nv_bfloat162 v =
-            __floats2bfloat162_rn(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1]));
-        h[i] = *reinterpret_cast<uint32_t*>(&v);
-    }
-    store_words<16>(dst, h, align32);
+// Store one converted row chunk (32 columns starting at `col` of output row `row`) into every
+// destination of the list.
+template <typename OutT>
+__device__ __forceinline__ void store_chunk_all(const DstList& dl, int row, int col,
+                                                const uint32_t (&w)[ChunkWords<OutT>::N], bool align32) {
+    for (int d = 0; d < dl.n; d++)
+        store_words<ChunkWords<OutT>::N>(static_cast<OutT*>(dl.p[d]) + (size_t)row * dl.ldd + dl.col0 + col, w,
+                                        align32);
 }
 
 // OutT: float / __half / __nv_bfloat16. PARTIAL: write FP32 partial sums to p.ws instead of D.
@@ -387,10 +403,11 @@ __global__ void __launch_bounds__(threads_for(AMODE), 1)
                 if (row < p.M) {
                     if constexpr (PARTIAL) {
                         float* dst = p.ws + ((size_t)tc.split * p.M + row) * p.N + col0 + c;
-                        store_row_chunk<float>(dst, r, p.out_align32 != 0);
+                        store_words<32>(dst, r, p.out_align32 != 0);
                     } else {
-                        OutT* dst = static_cast<OutT*>(p.D) + (size_t)row * p.N + col0 + c;
-                        store_row_chunk<OutT>(dst, r, p.out_align32 != 0);
+                        uint32_t w[ChunkWords<OutT>::N];
+                        convert_chunk<OutT>(r, w);
+                        store_chunk_all<OutT>(p.dst, row, col0 + c, w, p.out_align32 != 0);
                     }
                 }
             }
@@ -410,9 +427,10 @@ __global__ void __launch_bounds__(threads_for(AMODE), 1)
 }
 
 // Split-K second stage (reference: src/kernel.hpp:305-313): D = sum_{s=0..S-1} ws[s], in that
-// fixed order, converted once. Four elements per thread per step (M*N % 4 == 0 always holds).
+// fixed order, converted once and written to every destination of the list. Four elements per
+// thread per step (N % 4 == 0, so the four stay in one row).
 template <typename OutT>
-__global__ void __launch_bounds__(256) reduce_partials(const float* __restrict__ ws, OutT* __restrict__ D,
+__global__ void __launch_bounds__(256) reduce_partials(const float* __restrict__ ws, const DstList dl, int N,
                                                        long long total, int S) {
     const long long n4 = total / 4;
     for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n4;
@@ -425,17 +443,21 @@ __global__ void __launch_bounds__(256) reduce_partials(const float* __restrict__
             acc.z += v.z;
             acc.w += v.w;
         }
+        const long long e = 4 * i;
+        const long long row = e / N;
+        const int col = (int)(e - row * N);
+        const size_t off = (size_t)row * dl.ldd + dl.col0 + col;
         if constexpr (std::is_same<OutT, float>::value) {
-            reinterpret_cast<float4*>(D)[i] = acc;
+            for (int d = 0; d < dl.n; d++) *reinterpret_cast<float4*>(static_cast<float*>(dl.p[d]) + off) = acc;
         } else if constexpr (std::is_same<OutT, __half>::value) {
             __half2 lo = __floats2half2_rn(acc.x, acc.y), hi = __floats2half2_rn(acc.z, acc.w);
-            uint2 o = make_uint2(*reinterpret_cast<uint32_t*>(&lo), *reinterpret_cast<uint32_t*>(&hi));
-            reinterpret_cast<uint2*>(D)[i] = o;
+            const uint2 o = make_uint2(*reinterpret_cast<uint32_t*>(&lo), *reinterpret_cast<uint32_t*>(&hi));
+            for (int d = 0; d < dl.n; d++) *reinterpret_cast<uint2*>(static_cast<__half*>(dl.p[d]) + off) = o;
         } else {
-            __nv_bfloat162 lo = __floats2bfloat162_rn(acc.x, acc.y),
-                           hi = __floats2bfloat162_rn(acc.z, acc.w);
-            uint2 o = make_uint2(*reinterpret_cast<uint32_t*>(&lo), *reinterpret_cast<uint32_t*>(&hi));
-            reinterpret_cast<uint2*>(D)[i] = o;
+            __nv_bfloat162 lo = __floats2bfloat162_rn(acc.x, acc.y), hi = __floats2bfloat162_rn(acc.z, acc.w);
+            const uint2 o = make_uint2(*reinterpret_cast<uint32_t*>(&lo), *reinterpret_cast<uint32_t*>(&hi));
+            for (int d = 0; d < dl.n; d++)
+                *reinterpret_cast<uint2*>(static_cast<__nv_bfloat16*>(dl.p[d]) + off) = o;
         }
     }
 }

@@ -365,9 +365,11 @@ __global__ void __launch_bounds__(threads_for(AMODE), 1)
                 const int col = col0 + 32 * c;
                 if (row < p.M && col < p.N) {
                     if constexpr (PARTIAL) {
-                        store_row_chunk<float>(p.ws + ((size_t)tc.split * p.M + row) * p.N + col, r, p.out_align32 != 0);
+                        store_words<32>(p.ws + ((size_t)tc.split * p.M + row) * p.N + col, r, p.out_align32 != 0);
                     } else {
-                        store_row_chunk<OutT>(static_cast<OutT*>(p.D) + (size_t)row * p.N + col, r, p.out_align32 != 0);
+                        uint32_t w[ChunkWords<OutT>::N];
+                        convert_chunk<OutT>(r, w);
+                        store_chunk_all<OutT>(p.dst, row, col, w, p.out_align32 != 0);
                     }
                 }
             }

@@ -52,6 +52,15 @@ _static_ws_gemm = _fn("mxfp6_gemm_static_workspace", None,
                       [C.c_int, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
                        C.c_void_p, C.c_int, C.c_int, C.c_void_p])
 static_workspace_bytes = _fn("mxfp6_static_workspace_bytes", C.c_size_t, [])
+_gather = _fn("mxfp6_gemm_gather", None,
+              [C.c_int, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
+               C.POINTER(C.c_void_p), C.c_int, C.c_longlong, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_size_t,
+               C.c_void_p])
+_ipc_export = _fn("mxfp6_ipc_export", C.c_int, [C.c_void_p, C.c_void_p, C.POINTER(C.c_size_t)])
+_ipc_import = _fn("mxfp6_ipc_import", C.c_int, [C.c_void_p, C.c_size_t, C.POINTER(C.c_void_p),
+                                               C.POINTER(C.c_void_p)])
+_ipc_close = _fn("mxfp6_ipc_close", C.c_int, [C.c_void_p])
+
 _ws = _fn("mxfp6_gemm_workspace_size", C.c_size_t, [C.c_int, C.c_int, C.c_int])
 _ws_out = _fn("mxfp6_gemm_workspace_size_out", C.c_size_t, [C.c_int, C.c_int, C.c_int, C.c_int])
 _choose = _fn("mxfp6_choose_tile", None, [C.c_int, C.c_int, C.c_int, C.POINTER(C.c_int)])
@@ -152,6 +161,40 @@ def gemm_force_tile(ot, M, N, Kp, MT, NT, splits, dA, dBsh, dsA, dsB, dD, A_row_
     s = 0 if stream is None else (stream.cuda_stream if hasattr(stream, "cuda_stream") else _addr(stream))
     _force(int(ot), M, N, Kp, MT, NT, splits, _addr(dA), _addr(dBsh), _addr(dsA), _addr(dsB), _addr(dD),
            A_row_bytes, B_row_bytes, _addr(ws), ws_bytes, s)
+
+
+def gemm_gather(ot, M, N, Kp, dA, dBsh, dsA, dsB, dDs, ldd, col0, A_row_bytes, B_row_bytes, ws=None, ws_bytes=0,
+                stream=None):
+    """mxfp6_gemm_gather: D written into every destination of dDs (tensors or device addresses),
+    each a row-major [M][ldd] matrix, at column col0."""
+    ptrs = (C.c_void_p * len(dDs))(*[_addr(d) for d in dDs])
+    s = 0 if stream is None else (stream.cuda_stream if hasattr(stream, "cuda_stream") else _addr(stream))
+    _gather(int(ot), M, N, Kp, _addr(dA), _addr(dBsh), _addr(dsA), _addr(dsB), ptrs, len(dDs), ldd, col0,
+            A_row_bytes, B_row_bytes, _addr(ws), ws_bytes, s)
+
+
+def ipc_export(t) -> tuple[bytes, int]:
+    """(64-byte CUDA IPC handle of the allocation holding t, t's offset in it)."""
+    h = (C.c_uint8 * 64)()
+    off = C.c_size_t(0)
+    rc = _ipc_export(_addr(t), h, C.byref(off))
+    if rc != OK:
+        raise RuntimeError(f"mxfp6_ipc_export failed ({rc})")
+    return bytes(h), off.value
+
+
+def ipc_import(handle: bytes, offset: int) -> tuple[int, int]:
+    """Map a peer allocation: returns (base for ipc_close, device address of the tensor)."""
+    h = (C.c_uint8 * 64).from_buffer_copy(handle)
+    base, ptr = C.c_void_p(), C.c_void_p()
+    rc = _ipc_import(h, offset, C.byref(base), C.byref(ptr))
+    if rc != OK:
+        raise RuntimeError(f"mxfp6_ipc_import failed ({rc})")
+    return base.value, ptr.value
+
+
+def ipc_close(base: int) -> int:
+    return _ipc_close(base)
 
 
 def gemm_static_workspace(ot, M, N, Kp, dA, dBsh, dsA, dsB, dD, A_row_bytes, B_row_bytes, stream=None):

@@ -179,3 +179,20 @@ def test_forced_route_validation(lib, capfd):
     assert lib.last_error() == lib.ERR_UNSUPPORTED
     lib.gemm_force_tile(0, 128, 128, 512, 128, 128, 2, 0x1000, 0x2000, 0x3000, 0x4000, 0x5000, 384, 384, None, 0)
     assert lib.last_error() == lib.ERR_WORKSPACE
+
+
+def test_gather_validation(lib, capfd):
+    """mxfp6_gemm_gather rejects bad destination lists before any device work."""
+    args = dict(ot=1, M=128, N=128, Kp=128, dA=0x1000, dB=0x2000, dsA=0x3000, dsB=0x4000, Ar=96, Br=96)
+    base = (args["ot"], args["M"], args["N"], args["Kp"], args["dA"], args["dB"], args["dsA"], args["dsB"])
+    lib.gemm_gather(*base, [], 256, 0, 96, 96)
+    assert lib.last_error() == lib.ERR_NULL_POINTER
+    lib.gemm_gather(*base, [0x5000] * 9, 256, 0, 96, 96)
+    assert lib.last_error() == lib.ERR_NULL_POINTER
+    lib.gemm_gather(*base, [0x5000], 200, 128, 96, 96)          # ldd < col0 + N
+    assert lib.last_error() == lib.ERR_INVALID_STRIDE
+    lib.gemm_gather(*base, [0x5000], 260, 4, 96, 96)            # col0 * 2 bytes not 16-aligned
+    assert lib.last_error() == lib.ERR_INVALID_STRIDE
+    lib.gemm_gather(*base, [0x5000, 0x5008], 256, 0, 96, 96)    # second destination misaligned
+    assert lib.last_error() == lib.ERR_MISALIGNED
+    assert "[mxfp6]" in capfd.readouterr().err
