@@ -54,7 +54,7 @@ METRIC = "MXFP6 GEMM TFLOPS (2*M*N*K / device time)"
 L2_FLUSH_BYTES = 256 << 20
 # DRAM bytes (read + write) per launch of the dominant kernel, from one ncu capture of this
 # bench's own command (profiles/gemm_mxfp6_sm100_pair_cfg2.md); None where not captured yet.
-NCU_TRAFFIC_BYTES = {"cfg2": 256_694_272 + 117_018_112}
+NCU_TRAFFIC_BYTES = {"cfg2": 257_806_848 + 114_925_568}
 
 
 def load_peaks():
@@ -353,7 +353,7 @@ def run_ours(args):
 
     # ---- compact A (the reference's row stride 3K/4 with K % 128 != 0; loader-warp producer) ----
     compact = None
-    if world == 1 and K % 128 == 0 and K > 128:
+    if args.with_compact and world == 1 and K % 128 == 0 and K > 128:
         Kc = K - 32  # same Kp, so the same MMA work; A rows of 3*Kc/4 bytes
         rbc = Kc * 3 // 4
         Ac = A[:, :rbc].contiguous()
@@ -538,6 +538,8 @@ def main():
     ap.add_argument("--config", choices=sorted(CONFIGS), default="cfg2")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-allgather", action="store_true")
+    ap.add_argument("--with-compact", action="store_true",
+                    help="also time the same GEMM with A in the reference's compact layout (loader warps)")
     ap.add_argument("--ref-seconds", type=float, default=10.0, help="target CPU seconds per reference sample")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
