@@ -52,6 +52,7 @@ CONFIG_DESC = {
 }
 METRIC = "MXFP6 GEMM TFLOPS (2*M*N*K / device time)"
 L2_FLUSH_BYTES = 256 << 20
+E2E_CHUNKS = 8  # row chunks of the end-to-end step (copies overlap the GEMM)
 # DRAM bytes (read + write) per launch of the dominant kernel, from one ncu capture of this
 # bench's own command (profiles/gemm_mxfp6_sm100_pair_cfg2.md); None where not captured yet.
 NCU_TRAFFIC_BYTES = {"cfg2": 257_806_848 + 114_925_568}
@@ -299,13 +300,51 @@ def run_ours(args):
     h2d = sum(p.numel() * p.element_size() for p in pinned.values())
     d2h = Dh.numel() * Dh.element_size()
 
+    # The step's transfers and math overlap: B^T and its scales go up first, then A in row chunks
+    # on a copy stream; each chunk's GEMM (the public gemm() on that chunk's rows of A, its scale
+    # atoms and its rows of D) runs on the compute stream as soon as its rows have landed, and each
+    # D chunk goes back on a third stream as soon as it is computed. Every byte still crosses PCIe
+    # inside every step.
+    s_up = torch.cuda.Stream(dev)
+    s_down = torch.cuda.Stream(dev)
+    chunks = E2E_CHUNKS if M % (128 * E2E_CHUNKS) == 0 else 1
+    mc = M // chunks
+    sa_chunk = (mc // 128) * (Kp // 128) * 512  # scale atoms are row-block major
+    wsb_c = lib.gemm_workspace_size(mc, N, Kp, ot)  # a chunk's own route may split K
+    ws_c = torch.empty(max(wsb_c, 16), dtype=torch.uint8, device=dev)
+
     def e2e_step():
-        dA2.copy_(pinned["A"], non_blocking=True)
-        dB2.copy_(pinned["Bt"], non_blocking=True)
-        dsA2.copy_(pinned["sA"], non_blocking=True)
-        dsB2.copy_(pinned["sB"], non_blocking=True)
-        lib.gemm(ot, M, N, Kp, dA2, dB2, dsA2, dsB2, D, rb, rb, ws if wsb else None, wsb, stream=stream)
-        Dh.copy_(D, non_blocking=True)
+        ev_start = torch.cuda.Event()
+        ev_start.record(stream)
+        s_up.wait_event(ev_start)
+        with torch.cuda.stream(s_up):
+            dB2.copy_(pinned["Bt"], non_blocking=True)
+            dsB2.copy_(pinned["sB"], non_blocking=True)
+            up = []
+            for c in range(chunks):
+                r0, r1 = c * mc, (c + 1) * mc
+                dA2[r0:r1].copy_(pinned["A"][r0:r1], non_blocking=True)
+                dsA2[c * sa_chunk:(c + 1) * sa_chunk].copy_(pinned["sA"][c * sa_chunk:(c + 1) * sa_chunk],
+                                                            non_blocking=True)
+                ev = torch.cuda.Event()
+                ev.record(s_up)
+                up.append(ev)
+        done = []
+        for c in range(chunks):
+            r0, r1 = c * mc, (c + 1) * mc
+            stream.wait_event(up[c])
+            lib.gemm(ot, mc, N, Kp, dA2[r0:r1], dB2, dsA2[c * sa_chunk:], dsB2, D[r0:r1], rb, rb,
+                     ws_c if wsb_c else None, wsb_c, stream=stream)
+            ev = torch.cuda.Event()
+            ev.record(stream)
+            done.append(ev)
+        with torch.cuda.stream(s_down):
+            for c in range(chunks):
+                s_down.wait_event(done[c])
+                Dh[c * mc:(c + 1) * mc].copy_(D[c * mc:(c + 1) * mc], non_blocking=True)
+        ev_end = torch.cuda.Event()
+        ev_end.record(s_down)
+        stream.wait_event(ev_end)
 
     e2e_steps = max(3, min(args.steps, 20))
     for _ in range(2):
@@ -512,7 +551,9 @@ def run_ours(args):
                          "best_step_ms": kernel_ms},
             "cpu_baseline": cpu,
             "e2e": {"value": e2e_value, "unit": "TFLOPS", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                    "ms_per_step": e2e_ms, "path": "pinned host -> H2D copies -> mxfp6_gemm (C ABI) -> D2H"},
+                    "ms_per_step": e2e_ms,
+                    "path": f"pinned host -> H2D (B^T, scales, then A in {chunks} row chunks) overlapped with "
+                            f"mxfp6_gemm_stream (C ABI) per row chunk, overlapped with D2H per row chunk"},
             "gpu_launches": launches,
             "clocks": clk.summary(),
             "device_status": status,
