@@ -95,10 +95,6 @@ __device__ __forceinline__ void cp_async_4(uint32_t dst, const void* src, uint32
     asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
 }
 
-__device__ __forceinline__ void cp_async_commit() {
-    asm volatile("cp.async.commit_group;" ::: "memory");
-}
-
 __device__ __forceinline__ void cp_async_wait_all() {
     asm volatile("cp.async.wait_all;" ::: "memory");
 }
@@ -123,12 +119,6 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const void* tmap, uint
         " [%0], [%1, {%3, %4}], [%2];" ::"r"(dst),
         "l"(tmap), "r"(bar), "r"(c0), "r"(c1)
         : "memory");
-}
-
-// Prefetch a 2-D box of a tensor map into L2 (no shared-memory destination, no completion).
-__device__ __forceinline__ void tma_prefetch_2d(const void* tmap, int c0, int c1) {
-    asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global [%0, {%1, %2}];" ::"l"(tmap), "r"(c0), "r"(c1)
-                 : "memory");
 }
 
 // Untiled bulk copy global -> shared (16-byte aligned addresses, size a multiple of 16).
@@ -274,29 +264,6 @@ __device__ __forceinline__ void cluster_sync() {
 // Arrive on an mbarrier of any CTA in the cluster (shared::cluster address).
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_bar) {
     asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar) : "memory");
-}
-
-__device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t parity) {
-    uint32_t ok;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(ok)
-        : "r"(bar), "r"(parity)
-        : "memory");
-    return ok != 0;
-}
-
-__device__ __forceinline__ bool wait_parity_bounded_cluster(uint32_t bar, uint32_t parity,
-                                                            const volatile int* abort, long long budget) {
-    if (mbar_try_wait_cluster(bar, parity)) return true;
-    const long long t0 = clock64();
-    while (true) {
-        if (mbar_try_wait_cluster(bar, parity)) return true;
-        if (*abort) return false;
-        if (clock64() - t0 > budget) return false;
-    }
 }
 
 // Tensor loads into this CTA's shared memory that complete on an mbarrier of either CTA of the
