@@ -113,3 +113,35 @@ def test_padded_output_rows(lib, rows, cols, tiled):
         assert np.array_equal(s, lib.preprocess_scale(want, rows, Kp))
     else:
         assert np.array_equal(s.reshape(rows, Kp // 32), want)
+
+
+@pytest.mark.parametrize("M,N,K", [(512, 768, 1952), (1024, 512, 8192)])
+def test_activation_path_on_device(lib, oracle, M, N, K):
+    """The FFN step on the device: FP32 activations -> quantize_device_padded (rows of kpad(K)
+    codes, GEMM-tiled scales) -> GEMM, with no host round trip; equals the oracle GEMM of the
+    host quantiser's output (A zero-padded to kpad(K))."""
+    from gpu_helpers import check
+    from mxfp6_b200.synth import make_operands
+    rng = np.random.default_rng(M + N + K)
+    x = rng.standard_normal((M, K)).astype(np.float32)
+    Kp = lib.kpad(K)
+    b = make_operands(128, N, K, kind="normal", seed=5, sigma=(1.0, 0.02))
+    d_x = torch.from_numpy(x).cuda()
+    a_packed = torch.empty((M, Kp * 3 // 4), dtype=torch.uint8, device="cuda")
+    a_scales = torch.empty(lib.tiled_scale_bytes(M, Kp), dtype=torch.uint8, device="cuda")
+    assert lib.quantize_device_padded(d_x, M, K, Kp, a_packed, a_scales, True) == lib.OK
+    Bt = torch.from_numpy(b.Bt).cuda()
+    sB = torch.from_numpy(lib.preprocess_scale(b.sB, N, Kp)).cuda()
+    D = torch.empty((M, N), dtype=torch.float32, device="cuda")
+    wsb = lib.gemm_workspace_size(M, N, Kp, lib.OutType.F32)
+    ws = torch.empty(max(wsb, 16), dtype=torch.uint8, device="cuda") if wsb else None
+    lib.gemm(lib.OutType.F32, M, N, Kp, a_packed, Bt, a_scales, sB, D, Kp * 3 // 4, Kp * 3 // 4, ws, wsb)
+    assert lib.last_error() == lib.OK
+    torch.cuda.synchronize()
+    assert lib.device_status() == 0
+    host = lib.quantize_to_mxfp6(x)
+    A_pad = np.zeros((M, Kp * 3 // 4), np.uint8)
+    A_pad[:, :K * 3 // 4] = host.packed_data
+    sA_pad = lib.pad_scales_k(host.scales, M, K)
+    assert np.array_equal(a_packed.cpu().numpy(), A_pad)
+    check(D.cpu(), oracle.gemm(A_pad, sA_pad, b.Bt, b.sB, Kp), lib.OutType.F32, oracle, label=f"ffn {M}x{N}x{K}")
