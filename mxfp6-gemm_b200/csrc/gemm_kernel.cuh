@@ -179,6 +179,43 @@ __device__ __forceinline__ void store_chunk_all(const DstList& dl, int row, int 
                                         align32);
 }
 
+// Output staging for several destinations (the fused gather): per epilogue warp a [32 rows] x
+// [128 + 16 bytes] shared-memory area, the 16 padding bytes spreading a warp's row writes over
+// all banks.
+constexpr int EPI_STG_PITCH = 144;
+constexpr int EPI_STG_WARP = 32 * EPI_STG_PITCH;
+constexpr int EPI_STG_BYTES = 4 * EPI_STG_WARP;
+
+// Multi-destination store of 128 bytes per row: lane l holds 32 words of row row0 + l starting
+// at column `col` (32 FP32 or 64 FP16/BF16 columns). The warp regroups them through its staging
+// area so that in each store instruction four lanes write one row's 128 bytes as consecutive
+// 32-byte pieces: every destination, local or a peer's over NVLink, receives 128-byte runs
+// instead of one 32-byte piece per row and instruction. Rows at or past M are skipped.
+template <typename OutT>
+__device__ __forceinline__ void store_rows_regrouped(const DstList& dl, uint8_t* stg, int row0, int M, int col,
+                                                     const uint32_t (&w)[32], bool align32) {
+    const int lane = threadIdx.x & 31;
+    uint4* mine = reinterpret_cast<uint4*>(stg + lane * EPI_STG_PITCH);
+#pragma unroll
+    for (int i = 0; i < 8; i++) mine[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+    __syncwarp();
+    const int k = lane >> 2, j = lane & 3;
+    constexpr int COLS_PER_32B = 32 / (int)sizeof(OutT);
+#pragma unroll
+    for (int q = 0; q < 4; q++) {
+        const int r = 8 * q + k;
+        const uint4* src = reinterpret_cast<const uint4*>(stg + r * EPI_STG_PITCH + 32 * j);
+        const uint4 a = src[0], b = src[1];
+        const uint32_t v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+        const int row = row0 + r;
+        if (row < M)
+            for (int d = 0; d < dl.n; d++)
+                store_words<8>(static_cast<OutT*>(dl.p[d]) + (size_t)row * dl.ldd + dl.col0 + col + COLS_PER_32B * j,
+                               v, align32);
+    }
+    __syncwarp();  // the staging area is rewritten by the next group
+}
+
 // OutT: float / __half / __nv_bfloat16. PARTIAL: write FP32 partial sums to p.ws instead of D.
 // AMODE (compact_a.cuh): A_TMA loads A with the 16U6 tensor load; A_CPASYNC adds four
 // loader warps that copy the A image from p.a_ptr (tmA unused).

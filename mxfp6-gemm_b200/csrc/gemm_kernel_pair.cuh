@@ -51,7 +51,7 @@ struct PairConfig {
     static_assert(TMEM_SF + SUB * SF_SET_COLS <= 512, "tensor memory budget");
     static constexpr int EPI_WARPS = 4;
     static constexpr int BAR_BYTES = 256;
-    static constexpr int SMEM_BYTES = 1024 + STAGES * (AB_STAGE + SF_STAGE) + BAR_BYTES;
+    static constexpr int SMEM_BYTES = 1024 + STAGES * (AB_STAGE + SF_STAGE) + BAR_BYTES + EPI_STG_BYTES;
     static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
 };
 
@@ -87,6 +87,7 @@ __global__ void __launch_bounds__(threads_for(AMODE), 1)
     const uint32_t ovl_free = acc_full0 + 32u;
     const uint32_t drain_bar = acc_full0 + 40u;
     const int slot_off = 8 * (2 * C::STAGES + 6);
+    uint8_t* epi_stg = bar_ptr + C::BAR_BYTES;  // EPI_STG_BYTES: output regrouping (several destinations)
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_ptr + slot_off);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(bar_ptr + slot_off + 8);
 
@@ -349,6 +350,8 @@ __global__ void __launch_bounds__(threads_for(AMODE), 1)
             sm100::tc_fence_after();
             const int row = tc.mb * C::BM + 128 * (int)rank + 32 * quarter + lane;
             const int col0 = tc.nb * C::BN;
+            const bool regroup = !PARTIAL && p.dst.n > 1;
+            uint32_t pend[16];  // FP16/BF16 with several destinations: first chunk of a 64-column pair
 #pragma unroll 1
             for (int j = 0; j < C::BN / 32; j++) {
                 // buffer 0 top-down, buffer 1 bottom-up: the shared chunk [224, 256) goes first
@@ -363,7 +366,33 @@ __global__ void __launch_bounds__(threads_for(AMODE), 1)
                     if (lane == 0) sm100::mbar_arrive_cluster(leader_ovl_free);
                 }
                 const int col = col0 + 32 * c;
-                if (row < p.M && col < p.N) {
+                if (regroup) {
+                    // chunks are processed in pairs (c, c ^ 1) in both orders; col < N is uniform
+                    if (col < p.N) {
+                        uint8_t* stg = epi_stg + quarter * EPI_STG_WARP;
+                        const int row0 = row - lane;
+                        if constexpr (std::is_same<OutT, float>::value) {
+                            store_rows_regrouped<float>(p.dst, stg, row0, p.M, col, r, p.out_align32 != 0);
+                        } else {
+                            uint32_t w[16];
+                            convert_chunk<OutT>(r, w);
+                            if ((j & 1) == 0) {
+#pragma unroll
+                                for (int i = 0; i < 16; i++) pend[i] = w[i];
+                            } else {
+                                const bool lower_first = (c ^ 1) < c;  // the pending chunk holds the lower columns
+                                uint32_t w32[32];
+#pragma unroll
+                                for (int i = 0; i < 16; i++) {
+                                    w32[i] = lower_first ? pend[i] : w[i];
+                                    w32[16 + i] = lower_first ? w[i] : pend[i];
+                                }
+                                store_rows_regrouped<OutT>(p.dst, stg, row0, p.M, col0 + 32 * (c & ~1), w32,
+                                                           p.out_align32 != 0);
+                            }
+                        }
+                    }
+                } else if (row < p.M && col < p.N) {
                     if constexpr (PARTIAL) {
                         store_words<32>(p.ws + ((size_t)tc.split * p.M + row) * p.N + col, r, p.out_align32 != 0);
                     } else {
