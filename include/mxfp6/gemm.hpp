@@ -46,6 +46,13 @@ TileChoice choose_tile(int M, int N, int Kp);
 // The caller owns this device buffer (allocate once, reuse across calls, one per stream).
 size_t gemm_workspace_size(int M, int N, int Kp);
 
+// The same for an A of row stride A_row_bytes (no counterpart in the reference): when that stride
+// is not one the tensor load can address (the compact 3K/4 with K % 128 != 0), the size adds room
+// for a padded copy of A, which gemm() then makes (one HBM pass) before running the tensor-load
+// kernel. A workspace sized by the three-argument query still works for such an A: the kernels'
+// loader warps then read it in place, with identical results, at about 0.57 of the speed.
+size_t gemm_workspace_size(int M, int N, int Kp, int A_row_bytes);
+
 // D[M,N] = A[M,K] * B[K,N]; see the layout notes above. Requirements (checked; a violation
 // prints "[mxfp6] ..." to stderr, records an error for mxfp6_last_error() and launches nothing):
 //   M % 128 == 0, N % 128 == 0, Kp % 128 == 0, Kp > 0; B_row_bytes >= 0.75*Kp and a multiple of

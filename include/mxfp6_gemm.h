@@ -80,6 +80,11 @@ size_t mxfp6_gemm_workspace_size(int M, int N, int Kp);
  * allocate exactly what that call uses. */
 size_t mxfp6_gemm_workspace_size_out(int ot, int M, int N, int Kp);
 
+/* Workspace for an A of row stride A_row_bytes (no counterpart in the reference): adds room for
+ * a padded copy of A when the stride is one the tensor load cannot address (the compact 3K/4),
+ * so that mxfp6_gemm re-pads A into the workspace and runs the tensor-load kernel. */
+size_t mxfp6_gemm_workspace_size_a(int M, int N, int Kp, int A_row_bytes);
+
 /* Column-parallel GEMM whose epilogue also performs the all-gather of the shards (no
  * counterpart in the reference, whose multi-GPU use is left to the caller): D = A·B (this
  * rank's N columns) is written into each of the n_dst (1..8) row-major [M][ldd] matrices dDs[i]

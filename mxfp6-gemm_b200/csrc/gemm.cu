@@ -23,6 +23,10 @@
 
 namespace mxfp6 {
 
+cudaError_t launch_repad(const uint8_t* src, int rows, int src_row_bytes, int bytes_used, uint8_t* dst,
+                         int dst_row_bytes, cudaStream_t stream);  // quantize.cu
+void note_launch();
+
 namespace {
 
 thread_local int t_last_error = MXFP6_OK;
@@ -397,6 +401,15 @@ Route route_for_out(int ot, int M, int N, int Kp) {
     return route_for(M, N, Kp, sm_count(), ot == MXFP6_OUT_F32 ? fp32_min_splits(Kp) : 1);
 }
 
+// Bytes of a padded copy of A (rows of 0.75*Kp) placed after the split-K partials in the
+// workspace; the offset keeps the copy 256-byte aligned for the tensor load.
+size_t padded_a_bytes(int M, int Kp) {
+    return (size_t)M * (size_t)(Kp / 4 * 3);
+}
+size_t padded_a_offset(size_t split_bytes) {
+    return (split_bytes + 255) / 256 * 256;
+}
+
 void gemm_entry(int ot, int M, int N, int Kp, const void* dA, const void* dB, const uint8_t* sA,
                 const uint8_t* sB, const kern::DstList& dl, int Ar, int Br, void* ws, size_t ws_bytes,
                 cudaStream_t stream) {
@@ -412,6 +425,26 @@ void gemm_entry(int ot, int M, int N, int Kp, const void* dA, const void* dB, co
                          "running unsplit (slower). Size it with gemm_workspace_size().\n",
                          M, N, Kp, ws_bytes, need);
             r.splits = 1;
+        }
+    }
+    // An A the tensor load cannot address (the compact stride 3K/4 with K % 128 != 0) is re-padded
+    // into the workspace, after the split-K partials, when the caller sized the workspace for it
+    // (gemm_workspace_size with A_row_bytes): one HBM pass, then the tensor-load kernel. Otherwise
+    // the kernels' loader warps read it in place (same results, slower).
+    if (a_mode(Kp, dA, Ar) == kern::A_CPASYNC && ws && aligned(ws, 256)) {
+        const size_t off = padded_a_offset(r.splits > 1 ? splitk_bytes(M, N, r.splits) : 0);
+        const int prb = Kp / 4 * 3;
+        if (ws_bytes >= off + padded_a_bytes(M, Kp)) {
+            uint8_t* pa = static_cast<uint8_t*>(ws) + off;
+            const cudaError_t e = launch_repad(static_cast<const uint8_t*>(dA), M, Ar, Ar < prb ? Ar : prb, pa, prb,
+                                               stream);
+            if (e != cudaSuccess) {
+                set_error(MXFP6_ERR_CUDA, "A re-pad launch failed: %s", cudaGetErrorString(e));
+                return;
+            }
+            note_launch();
+            dA = pa;
+            Ar = prb;
         }
     }
     run(ot, r, M, N, Kp, dA, dB, sA, sB, dl, Ar, Br, ws, stream);
@@ -464,6 +497,12 @@ size_t gemm_workspace_size(int M, int N, int Kp) {
     return need;
 }
 
+size_t gemm_workspace_size(int M, int N, int Kp, int A_row_bytes) {
+    const size_t split = gemm_workspace_size(M, N, Kp);
+    const bool tma_stride = A_row_bytes % 32 == 0 && (long long)A_row_bytes >= (long long)Kp * 3 / 4;
+    return tma_stride ? split : padded_a_offset(split) + padded_a_bytes(M, Kp);
+}
+
 void gemm(OutType ot, int M, int N, int Kp, const void* dA, const void* dBsh, const uint8_t* dsA,
           const uint8_t* dsB, void* dD, int A_row_bytes, int B_row_bytes, void* ws, size_t ws_bytes) {
     gemm_entry((int)ot, M, N, Kp, dA, dBsh, dsA, dsB, single_dst(dD, N), A_row_bytes, B_row_bytes, ws, ws_bytes,
@@ -493,6 +532,10 @@ void mxfp6_gemm_stream(int ot, int M, int N, int Kp, const void* dA, const void*
 
 size_t mxfp6_gemm_workspace_size(int M, int N, int Kp) {
     return gemm_workspace_size(M, N, Kp);
+}
+
+size_t mxfp6_gemm_workspace_size_a(int M, int N, int Kp, int A_row_bytes) {
+    return gemm_workspace_size(M, N, Kp, A_row_bytes);
 }
 
 size_t mxfp6_gemm_workspace_size_out(int ot, int M, int N, int Kp) {

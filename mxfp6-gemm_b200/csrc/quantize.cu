@@ -166,26 +166,42 @@ __global__ void pad_tail_kernel(int rows, int row_bytes, uint8_t* __restrict__ p
 }
 
 // Copy rows between strides, zero-filling each destination row past bytes_used (re-padding
-// compact operand rows for the tensor-memory accelerator). One block per row, 16-byte stores
-// when both strides allow, else bytes.
-__global__ void repad_kernel(const uint8_t* __restrict__ src, int rows, int src_row_bytes, int bytes_used,
-                             uint8_t* __restrict__ dst, int dst_row_bytes) {
+// compact operand rows for the tensor-memory accelerator). One block per row, in units of U
+// bytes: the largest of 16, 8, 4, 1 that divides both bases, both strides and bytes_used, so
+// that a compact stride of 3K/4 (a multiple of 8) still moves 8-byte words. HBM bound.
+template <typename U>
+__global__ void __launch_bounds__(256) repad_kernel(const uint8_t* __restrict__ src, int rows, int src_row_bytes,
+                                                    int bytes_used, uint8_t* __restrict__ dst, int dst_row_bytes) {
     const int row = blockIdx.x;
     if (row >= rows) return;
-    const uint8_t* s = src + (size_t)row * src_row_bytes;
-    uint8_t* d = dst + (size_t)row * dst_row_bytes;
-    const bool vec = ((reinterpret_cast<uintptr_t>(s) | reinterpret_cast<uintptr_t>(d)) & 15) == 0;
-    int i = 0;
-    if (vec) {
-        for (i = 16 * threadIdx.x; i + 16 <= bytes_used; i += 16 * blockDim.x)
-            *reinterpret_cast<uint4*>(d + i) = *reinterpret_cast<const uint4*>(s + i);
-        i = bytes_used / 16 * 16;
-    }
-    for (int j = i + threadIdx.x; j < bytes_used; j += blockDim.x) d[j] = s[j];
-    for (int j = bytes_used + threadIdx.x; j < dst_row_bytes; j += blockDim.x) d[j] = 0;
+    const U* s = reinterpret_cast<const U*>(src + (size_t)row * src_row_bytes);
+    U* d = reinterpret_cast<U*>(dst + (size_t)row * dst_row_bytes);
+    const int used = bytes_used / (int)sizeof(U), total = dst_row_bytes / (int)sizeof(U);
+    for (int i = threadIdx.x; i < used; i += blockDim.x) d[i] = __ldcs(s + i);
+    U zero;
+    memset(&zero, 0, sizeof(U));
+    for (int i = used + threadIdx.x; i < total; i += blockDim.x) d[i] = zero;
 }
 
 }  // namespace
+
+// Launch the re-pad copy with the widest unit the pointers and strides allow (used by
+// mxfp6_repad_rows_device and by gemm() for compact A with a large enough workspace).
+cudaError_t launch_repad(const uint8_t* src, int rows, int src_row_bytes, int bytes_used, uint8_t* dst,
+                         int dst_row_bytes, cudaStream_t stream) {
+    const uintptr_t a = reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(dst) |
+                        (uintptr_t)src_row_bytes | (uintptr_t)dst_row_bytes | (uintptr_t)bytes_used;
+    if ((a & 15) == 0)
+        repad_kernel<uint4><<<rows, 256, 0, stream>>>(src, rows, src_row_bytes, bytes_used, dst, dst_row_bytes);
+    else if ((a & 7) == 0)
+        repad_kernel<uint2><<<rows, 256, 0, stream>>>(src, rows, src_row_bytes, bytes_used, dst, dst_row_bytes);
+    else if ((a & 3) == 0)
+        repad_kernel<uint32_t><<<rows, 256, 0, stream>>>(src, rows, src_row_bytes, bytes_used, dst, dst_row_bytes);
+    else
+        repad_kernel<uint8_t><<<rows, 256, 0, stream>>>(src, rows, src_row_bytes, bytes_used, dst, dst_row_bytes);
+    return cudaGetLastError();
+}
+
 }  // namespace mxfp6
 
 extern "C" int mxfp6_quantize_device_padded(const float* d_mat, int rows, int cols, int padded_cols, uint8_t* d_packed,
@@ -241,10 +257,10 @@ extern "C" int mxfp6_repad_rows_device(const void* d_src, int rows, int src_row_
         std::fprintf(stderr, "[mxfp6] repad_rows_device: invalid arguments\n");
         return MXFP6_ERR_INVALID_STRIDE;
     }
-    repad_kernel<<<rows, 128, 0, static_cast<cudaStream_t>(stream)>>>(static_cast<const uint8_t*>(d_src), rows,
-                                                                     src_row_bytes, bytes_used,
-                                                                     static_cast<uint8_t*>(d_dst), dst_row_bytes);
-    cudaError_t e = cudaGetLastError();
+    const cudaError_t le = launch_repad(static_cast<const uint8_t*>(d_src), rows, src_row_bytes, bytes_used,
+                                        static_cast<uint8_t*>(d_dst), dst_row_bytes,
+                                        static_cast<cudaStream_t>(stream));
+    cudaError_t e = le;
     if (e != cudaSuccess) {
         std::fprintf(stderr, "[mxfp6] repad_rows_device launch failed: %s\n", cudaGetErrorString(e));
         return MXFP6_ERR_CUDA;

@@ -63,6 +63,7 @@ _ipc_close = _fn("mxfp6_ipc_close", C.c_int, [C.c_void_p])
 
 _ws = _fn("mxfp6_gemm_workspace_size", C.c_size_t, [C.c_int, C.c_int, C.c_int])
 _ws_out = _fn("mxfp6_gemm_workspace_size_out", C.c_size_t, [C.c_int, C.c_int, C.c_int, C.c_int])
+_ws_a = _fn("mxfp6_gemm_workspace_size_a", C.c_size_t, [C.c_int, C.c_int, C.c_int, C.c_int])
 _choose = _fn("mxfp6_choose_tile", None, [C.c_int, C.c_int, C.c_int, C.POINTER(C.c_int)])
 _k_tile = _fn("mxfp6_k_tile", C.c_int, [])
 _kpad = _fn("mxfp6_kpad", C.c_int, [C.c_int])
@@ -134,6 +135,11 @@ def choose_tile(M: int, N: int, Kp: int) -> TileChoice:
 def gemm_workspace_size(M: int, N: int, Kp: int, ot=None) -> int:
     """Split-K workspace bytes: for every output type (as the reference's query), or for `ot`."""
     return _ws(M, N, Kp) if ot is None else _ws_out(int(ot), M, N, Kp)
+
+
+def gemm_workspace_size_a(M: int, N: int, Kp: int, a_row_bytes: int) -> int:
+    """Workspace that also holds a padded copy of an A the tensor load cannot address."""
+    return _ws_a(M, N, Kp, a_row_bytes)
 
 
 def _addr(x) -> int:

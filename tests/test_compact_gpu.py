@@ -145,3 +145,34 @@ def test_device_repad_then_tensor_path(lib):
     D_c = _run(lib, ops, dA, stride, lib.OutType.BF16, dev)
     D_p = _run(lib, ops, padded, ops.row_bytes, lib.OutType.BF16, dev)
     assert torch.equal(D_c.view(torch.int16), D_p.view(torch.int16))
+
+
+@pytest.mark.parametrize("ot", ["F32", "BF16"])
+@pytest.mark.parametrize("M,N,K", [(4096, 4096, 224), (2048, 1024, 3808), (1152, 1280, 2144)])
+def test_compact_with_a_aware_workspace(lib, ot, M, N, K):
+    """With a workspace sized by gemm_workspace_size(M, N, Kp, A_row_bytes), gemm() re-pads the
+    compact A into the workspace (one extra launch) and runs the tensor-load kernel: the result
+    is bit-identical to the in-place loader path and to the padded A, and A is left untouched."""
+    ops, dev = _setup(M, N, K, kind="codes")
+    dA, stride = _compact_buffer(ops)
+    before = dA.clone()
+    o = lib.OutType[ot]
+    wsb = lib.gemm_workspace_size_a(M, N, ops.Kp, stride)
+    assert wsb >= M * ops.row_bytes
+    ws = torch.empty(wsb, dtype=torch.uint8, device="cuda")
+    D = torch.empty((M, N), dtype={0: torch.float32, 2: torch.bfloat16}[int(o)], device="cuda")
+    n0 = lib.launch_count()
+    lib.gemm(o, M, N, ops.Kp, dA, dev.Bt, dev.sA, dev.sB, D, stride, ops.row_bytes, ws, wsb)
+    assert lib.last_error() == lib.OK, lib.last_error_string()
+    torch.cuda.synchronize()
+    assert lib.device_status() == 0
+    n_repad = lib.launch_count() - n0
+    D_in_place = _run(lib, ops, dA, stride, o, dev)       # workspace from the 3-argument query
+    n1 = lib.launch_count()
+    _run(lib, ops, dA, stride, o, dev)
+    n_in_place = lib.launch_count() - n1
+    D_pad = _run(lib, ops, dev.A, ops.row_bytes, o, dev)
+    assert n_repad == n_in_place + 1
+    bits = (lambda t: t.view(torch.int32)) if o == lib.OutType.F32 else (lambda t: t.view(torch.int16))
+    assert torch.equal(bits(D.cpu()), bits(D_pad)) and torch.equal(bits(D_in_place), bits(D_pad))
+    assert torch.equal(dA, before)
