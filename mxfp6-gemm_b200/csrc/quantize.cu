@@ -7,9 +7,9 @@
 // It is the step before the GEMM for activations (the FFN's A operand), so it writes the scales
 // either raw [rows][cols/32] or directly in the GEMM's 128x4 atom layout.
 //
-// HBM bound: each element reads 4 bytes and writes 0.75 + 1/32. A warp quantises 128-element
-// chunks (four blocks, one float4 per lane), four chunks per warp with their loads in flight
-// together, and writes each chunk's 96 packed bytes as 24 aligned words.
+// Traffic: each element reads 4 bytes and writes 0.75 + 1/32. A warp quantises a 512-element
+// chunk: 16 consecutive values per lane (four float4 loads), a 32-value block per lane pair, and
+// each lane writes its own 12 packed bytes as three aligned words (quantize_kernel).
 #include <cuda_runtime.h>
 
 #include <atomic>
@@ -75,63 +75,60 @@ __device__ __forceinline__ float e8m0_reciprocal(uint32_t code) {
     return e > 0 ? __int_as_float(e << 23) : __int_as_float(0x00400000 >> (-e));
 }
 
-// Quantise one 128-element chunk held as one float4 per lane; returns the packed word this lane
-// writes (lanes 0..23) and the block's scale code (valid in every lane of the block).
-__device__ __forceinline__ uint32_t quantize_chunk(float4 x, int lane, uint32_t& code) {
-    float m = 0.0f;  // block max over 8 lanes; NaN never wins a > comparison
-    for (float a : {fabsf(x.x), fabsf(x.y), fabsf(x.z), fabsf(x.w)})
-        if (a > m) m = a;
-#pragma unroll
-    for (int off = 1; off < 8; off <<= 1) {
-        const float o = __shfl_xor_sync(0xffffffffu, m, off);
-        if (o > m) m = o;
-    }
-    code = scale_code(m);
-    const float inv = e8m0_reciprocal(code);
-    const uint32_t p01 = to_e2m3x2(x.y * inv, x.x * inv);  // code(x) | code(y) << 8
-    const uint32_t p23 = to_e2m3x2(x.w * inv, x.z * inv);
-    const uint32_t g = (p01 & 0x3Fu) | ((p01 >> 2) & 0xFC0u) | ((p23 & 0x3Fu) << 12) | ((p23 >> 2) & 0xFC0u) << 12;
-    // g: this lane's 3 bytes, codes x, y, z, w at bits 0, 6, 12, 18
-    // Bytes [3*lane, 3*lane + 3) of the chunk's 96; lane w < 24 packs word w = bytes [4w, 4w + 4).
-    const int lo = (4 * lane) / 3;
-    const uint32_t glo = __shfl_sync(0xffffffffu, g, lo & 31);
-    const uint32_t ghi = __shfl_sync(0xffffffffu, g, (lo + 1) & 31);
-    const int sh = 4 * lane - 3 * lo;  // byte offset of word w inside lane lo's 3 bytes (0..2)
-    return (glo >> (8 * sh)) | (ghi << (8 * (3 - sh)));
-}
-
-// One warp per (row, group of CHUNKS consecutive 128-element chunks); all loads of the group are
-// issued before any is used. Grid: x covers the chunk groups of a row, y the rows.
-constexpr int CHUNKS = 4;
-
+// One warp quantises a 512-element chunk of a row: lane l owns the 16 consecutive values
+// [16 l, 16 l + 16), so each 32-value block spans the lane pair (2b, 2b + 1) (one shuffle for its
+// max) and each lane packs its own 16 codes into 12 bytes = 3 words (bytes [12 l, 12 l + 12) of
+// the chunk's 384): no packing shuffles, and a warp's stores cover 384 contiguous bytes.
+// Grid: x covers the chunks of a row (8 warps per block), y the rows.
 __global__ void __launch_bounds__(256) quantize_kernel(const float* __restrict__ in, int rows, int cols,
                                                        uint8_t* __restrict__ packed, int out_row_bytes,
                                                        uint8_t* __restrict__ scales, int scale_cols, int tiled) {
     const int lane = threadIdx.x & 31;
-    const int group = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int chunk = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     const int row = blockIdx.y;
-    const int chunk0 = group * CHUNKS;
-    if (chunk0 * 128 >= cols || row >= rows) return;
-    const float* src = in + (size_t)row * cols;
-    float4 x[CHUNKS];
+    if (chunk * 512 >= cols || row >= rows) return;
+    const int col = chunk * 512 + 16 * lane;  // first of this lane's 16 values
+    const bool live = col < cols;             // cols % 32 == 0: a lane's 16 values are all in or all out
+    float v[16];
+    if (live) {
+        const float4* src = reinterpret_cast<const float4*>(in + (size_t)row * cols + col);
 #pragma unroll
-    for (int c = 0; c < CHUNKS; c++) {
-        const int col = (chunk0 + c) * 128 + 4 * lane;
-        x[c] = col < cols ? __ldcs(reinterpret_cast<const float4*>(src + col)) : make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int i = 0; i < 4; i++) {
+            const float4 q = __ldg(src + i);
+            v[4 * i] = q.x;
+            v[4 * i + 1] = q.y;
+            v[4 * i + 2] = q.z;
+            v[4 * i + 3] = q.w;
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < 16; i++) v[i] = 0.0f;
     }
-    const int row_bytes = cols / 4 * 3;
-    uint8_t* dst = packed + (size_t)row * out_row_bytes;
+    float m = 0.0f;  // fmaxf returns the other operand for a NaN: NaN never wins the max
 #pragma unroll
-    for (int c = 0; c < CHUNKS; c++) {
-        const int chunk = chunk0 + c;
-        if (chunk * 128 >= cols) break;  // uniform across the warp
-        uint32_t code;
-        const uint32_t word = quantize_chunk(x[c], lane, code);
-        const int valid = min(96, row_bytes - chunk * 96);  // a multiple of 24 (cols % 32 == 0)
-        if (lane < 24 && 4 * lane < valid)
-            *reinterpret_cast<uint32_t*>(dst + chunk * 96 + 4 * lane) = word;
-        const int col = chunk * 128 + 4 * lane;
-        if (col < cols && (lane & 7) == 0) {
+    for (int i = 0; i < 16; i++) m = fmaxf(m, fabsf(v[i]));
+    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
+    const uint32_t code = scale_code(m);
+    const float inv = e8m0_reciprocal(code);
+    uint32_t q[8];  // q[i] = code(v[2i]) | code(v[2i + 1]) << 8
+#pragma unroll
+    for (int i = 0; i < 8; i++) q[i] = to_e2m3x2(v[2 * i + 1] * inv, v[2 * i] * inv);
+    // codes c0..c15 (6 bits each) -> bits 6k of three words
+    uint32_t c[16];
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        c[2 * i] = q[i] & 0x3Fu;
+        c[2 * i + 1] = (q[i] >> 8) & 0x3Fu;
+    }
+    const uint32_t w0 = c[0] | (c[1] << 6) | (c[2] << 12) | (c[3] << 18) | (c[4] << 24) | (c[5] << 30);
+    const uint32_t w1 = (c[5] >> 2) | (c[6] << 4) | (c[7] << 10) | (c[8] << 16) | (c[9] << 22) | (c[10] << 28);
+    const uint32_t w2 = (c[10] >> 4) | (c[11] << 2) | (c[12] << 8) | (c[13] << 14) | (c[14] << 20) | (c[15] << 26);
+    if (live) {
+        uint32_t* dst = reinterpret_cast<uint32_t*>(packed + (size_t)row * out_row_bytes + (size_t)col / 4 * 3);
+        dst[0] = w0;
+        dst[1] = w1;
+        dst[2] = w2;
+        if ((lane & 1) == 0) {
             const int j = col / 32;  // block index in the row
             size_t off;
             if (tiled) {
@@ -224,9 +221,8 @@ extern "C" int mxfp6_quantize_device_padded(const float* d_mat, int rows, int co
         return MXFP6_ERR_INVALID_SHAPE;
     }
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    const int chunks = (cols + 127) / 128;
-    const int groups = (chunks + CHUNKS - 1) / CHUNKS;
-    dim3 grid((groups + 7) / 8, rows);
+    const int chunks = (cols + 511) / 512;
+    dim3 grid((chunks + 7) / 8, rows);
     quantize_kernel<<<grid, 256, 0, st>>>(d_mat, rows, cols, d_packed, out_row_bytes, d_scales, padded_cols / 32,
                                           scale_layout);
     cudaError_t e = cudaGetLastError();
