@@ -174,10 +174,20 @@ __global__ void __launch_bounds__(256) repad_kernel(const uint8_t* __restrict__ 
     const U* s = reinterpret_cast<const U*>(src + (size_t)row * src_row_bytes);
     U* d = reinterpret_cast<U*>(dst + (size_t)row * dst_row_bytes);
     const int used = bytes_used / (int)sizeof(U), total = dst_row_bytes / (int)sizeof(U);
-    for (int i = threadIdx.x; i < used; i += blockDim.x) d[i] = __ldcs(s + i);
+    const int bd = blockDim.x;
+    // four loads in flight per thread before their stores
+    for (int base = threadIdx.x; base < used; base += 4 * bd) {
+        U r[4];
+#pragma unroll
+        for (int k = 0; k < 4; k++)
+            if (base + k * bd < used) r[k] = __ldcs(s + base + k * bd);
+#pragma unroll
+        for (int k = 0; k < 4; k++)
+            if (base + k * bd < used) d[base + k * bd] = r[k];
+    }
     U zero;
     memset(&zero, 0, sizeof(U));
-    for (int i = used + threadIdx.x; i < total; i += blockDim.x) d[i] = zero;
+    for (int i = used + threadIdx.x; i < total; i += bd) d[i] = zero;
 }
 
 }  // namespace
