@@ -17,6 +17,12 @@
 //     next tile's MMAs may start as soon as that one chunk has left tensor memory; the rest of
 //     the epilogue runs under the next tile's main loop.
 //   * No TMA multicast anywhere: each CTA fetches its own operands.
+//   * A compact A (a row stride the 16U6 load cannot address) is copied into the A stages by
+//     four extra loader warps per CTA instead (AMODE = A_CPASYNC, compact_a.cuh).
+//   * The epilogue writes D to every destination of p.dst (one for a plain GEMM; this rank's and
+//     its peers' gathered outputs for mxfp6_gemm_gather). With several destinations each warp
+//     regroups its rows through a small shared-memory area so that every destination receives
+//     128-byte runs of a row (store_rows_regrouped).
 // Every wait is bounded (see gemm_kernel.cuh); a timeout also raises the peer's abort flag.
 #include "gemm_kernel.cuh"
 
