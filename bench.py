@@ -17,6 +17,10 @@ side; before every timed step a 256 MiB buffer is written to flush the 126 MB L2
 step's GEMM is bracketed by CUDA events on the launching stream; ms_per_step is the mean over
 the K steps, maximised over ranks. Clocks are sampled through NVML during the timed region.
 
+Extra keys: "timing_as_reference" repeats the measurement with the reference's own convention
+(8 warm-ups, 20 back-to-back calls, best of 4, no flush); --vs-cublas adds "vs_cublas_mxfp8",
+cuBLASLt's block-scaled MXFP8 GEMM on the same shape (burst, interleaved, and sustained).
+
 --impl reference times the reference's own CPU GEMM (mxfp6_gemm_ref, compiled from its sources
 into oracle/_ref) on the host cores, on a bounded row sample of the same workload; rank 0 only.
 """
@@ -56,6 +60,7 @@ E2E_CHUNKS = 8  # row chunks of the end-to-end step (copies overlap the GEMM)
 # DRAM bytes (read + write) per launch of the dominant kernel, from one ncu capture of this
 # bench's own command (profiles/gemm_mxfp6_sm100_pair_cfg2.md); None where not captured yet.
 NCU_TRAFFIC_BYTES = {"cfg2": 257_806_848 + 114_925_568}
+NOMINAL_FP6_TFLOPS = 4500.0  # B200 dense FP8/FP6 tensor rate, nominal (no sparsity)
 
 
 def load_peaks():
@@ -224,6 +229,77 @@ def run_reference_arm(args):
 
 
 # ---- our arm ----------------------------------------------------------------------------------------
+
+def run_vs_cublas(M, N, K, step, stream, flush, dev, rounds=6, burst=8, sustain_s=1.0):
+    """Context for the roofline: cuBLASLt's block-scaled MXFP8 GEMM (E4M3 operands, one E8M0
+    scale per 32 elements, the same tcgen05 instruction family and tensor rate as FP6) on the same
+    M, N, K with BF16 output, through torch's scaled_mm. Burst: the two kernels alternate in
+    rounds of `burst` L2-flushed launches so that clock and power drift affects both alike.
+    Sustained: each runs back to back for `sustain_s` seconds under NVML clock sampling (B200
+    settles under its power cap)."""
+    import torch
+    import torch.nn.functional as F
+
+    try:
+        a8 = (torch.randn(M, K, device=dev) * 0.5).to(torch.float8_e4m3fn)
+        b8 = (torch.randn(N, K, device=dev) * 0.5).to(torch.float8_e4m3fn).t()
+        nsa = (M + 127) // 128 * 128 * ((K // 32 + 3) // 4 * 4)
+        nsb = (N + 127) // 128 * 128 * ((K // 32 + 3) // 4 * 4)
+        sa = torch.full((nsa,), 127, dtype=torch.uint8, device=dev).view(torch.float8_e8m0fnu)
+        sb = torch.full((nsb,), 127, dtype=torch.uint8, device=dev).view(torch.float8_e8m0fnu)
+
+        def mx8():
+            return F.scaled_mm(a8, b8, sa, F.ScalingType.BlockWise1x32, sb, F.ScalingType.BlockWise1x32,
+                               F.SwizzleType.SWIZZLE_32_4_4, F.SwizzleType.SWIZZLE_32_4_4,
+                               output_dtype=torch.bfloat16)
+
+        for _ in range(3):
+            mx8()
+        torch.cuda.synchronize()
+    except Exception as e:  # no MX support in this torch / cuBLASLt: report, do not fail the bench
+        return {"unavailable": f"cuBLASLt MXFP8 via torch scaled_mm: {e!r}"[:300]}
+
+    fns = {"ours": step, "cublas_mxfp8": mx8}
+    times = {k: [] for k in fns}
+    for r in range(rounds):
+        for name in (fns if r % 2 == 0 else reversed(list(fns))):
+            for i in range(burst):
+                flush.fill_(i & 0xFF)
+                e0 = torch.cuda.Event(enable_timing=True)
+                e1 = torch.cuda.Event(enable_timing=True)
+                e0.record(stream)
+                fns[name]()
+                e1.record(stream)
+                torch.cuda.synchronize()
+                times[name].append(e0.elapsed_time(e1))
+    flop = 2.0 * M * N * K
+    out = {"what": "cuBLASLt block-scaled MXFP8 (E4M3 x E4M3, E8M0 per 32, BF16 out) on the same M, N, K",
+           "burst": {}, "sustained": {}}
+    for name, ts in times.items():
+        med = statistics.median(ts)
+        out["burst"][name] = {"median_ms": med, "tflops": flop / (med * 1e-3) / 1e12}
+    out["burst"]["ours_over_cublas"] = out["burst"]["ours"]["tflops"] / out["burst"]["cublas_mxfp8"]["tflops"]
+    for name, fn in fns.items():
+        torch.cuda.synchronize()
+        n, t0 = 0, time.time()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        with ClockSampler(dev.index or 0) as clk:
+            e0.record(stream)
+            while time.time() - t0 < sustain_s:
+                for _ in range(25):
+                    fn()
+                n += 25
+                e1.record(stream)
+                e1.synchronize()
+            e1.record(stream)
+            torch.cuda.synchronize()
+        per = e0.elapsed_time(e1) / n
+        out["sustained"][name] = {"ms": per, "tflops": flop / (per * 1e-3) / 1e12, "clocks": clk.summary()}
+    out["sustained"]["ours_over_cublas"] = (out["sustained"]["ours"]["tflops"]
+                                            / out["sustained"]["cublas_mxfp8"]["tflops"])
+    return out
+
 
 def run_ours(args):
     import torch
@@ -538,6 +614,28 @@ def run_ours(args):
         allgather["fused_gather"] = fused
         del gathered, gathered2
 
+    # ---- the reference's own timing convention (tests/test_gemm.cpp:32-52 of eeezio/mxfp6-gemm):
+    # 8 warm-ups, then 20 back-to-back calls between two events, best of 4 repetitions; no L2
+    # flush between calls, so operands that fit in L2 stay there ----
+    as_ref = None
+    if world == 1:
+        for _ in range(8):
+            step()
+        reps_ms = []
+        for _ in range(4):
+            r0 = torch.cuda.Event(enable_timing=True)
+            r1 = torch.cuda.Event(enable_timing=True)
+            r0.record(stream)
+            for _ in range(20):
+                step()
+            r1.record(stream)
+            torch.cuda.synchronize()
+            reps_ms.append(r0.elapsed_time(r1) / 20)
+        as_ref = {"ms": min(reps_ms), "tflops": 2.0 * M * N * K / (min(reps_ms) * 1e-3) / 1e12,
+                  "how": "8 warm-ups, 20 back-to-back calls between events, best of 4 (no L2 flush)"}
+
+    vs_cublas = run_vs_cublas(M, N, K, step, stream, flush, dev) if args.vs_cublas and world == 1 else None
+
     # ---- CPU baseline (rank 0, N=1 only) ----
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -551,6 +649,7 @@ def run_ours(args):
     kernel_ms = min(per)  # dominant kernel: the GEMM (plus the split-K reduce when routed)
     achieved = flops_rank / (ms * 1e-3) / 1e12
     route = lib.choose_tile(M, N, Kp)
+    splits = max(1, wsb // (M * N * 4))
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": "TFLOPS", "n_gpus": world, "steps": args.steps,
@@ -560,7 +659,7 @@ def run_ours(args):
             "config": {"workload": CONFIG_DESC[args.config] + (f", N-sharded over {world} GPUs (per-GPU shard N={N})"
                                                                if world > 1 else ""),
                        "M": M, "N_per_gpu": N, "N_total": N * world, "K": K, "out": out_name,
-                       "route": {"MT": route.MT, "NT": route.NT, "splits": max(1, wsb // (M * N * 4))},
+                       "route": {"MT": route.MT, "NT": route.NT, "splits": splits},
                        "parallelism": f"N-sharded x{world}, no collective on the GEMM path",
                        "l2": "256 MiB buffer written before every timed step (L2 flushed)"},
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
@@ -568,7 +667,10 @@ def run_ours(args):
                          "algorithmic_bytes": algo_bytes,
                          "peak_basis": f"2 x {basis} cuBLAS bf16 dense ({bf16_peak:.1f} TFLOP/s): B200's dense "
                                        f"FP8/FP6 tensor rate is twice bf16",
-                         "best_step_ms": kernel_ms},
+                         "best_step_ms": kernel_ms,
+                         "frac_of_nominal_fp6_dense": achieved / NOMINAL_FP6_TFLOPS,
+                         "algorithmic_gbs": algo_bytes / (ms * 1e-3) / 1e9,
+                         "splitk_workspace_bytes": 2 * splits * M * N * 4 if splits > 1 else 0},
             "cpu_baseline": cpu,
             "e2e": {"value": e2e_value, "unit": "TFLOPS", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "ms_per_step": e2e_ms,
@@ -584,6 +686,10 @@ def run_ours(args):
             line["quantize_device"] = quant
         if compact:
             line["compact_a"] = compact
+        if as_ref:
+            line["timing_as_reference"] = as_ref
+        if vs_cublas:
+            line["vs_cublas_mxfp8"] = vs_cublas
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
@@ -602,6 +708,9 @@ def main():
     ap.add_argument("--with-compact", action="store_true",
                     help="also time the same GEMM with A in the reference's compact layout (loader warps)")
     ap.add_argument("--ref-seconds", type=float, default=10.0, help="target CPU seconds per reference sample")
+    ap.add_argument("--vs-cublas", action="store_true",
+                    help="also time cuBLASLt's MXFP8 block-scaled GEMM on the same shape (interleaved "
+                         "with this library's, then each sustained for about a second with clocks)")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3
