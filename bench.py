@@ -56,7 +56,8 @@ CONFIG_DESC = {
 }
 METRIC = "MXFP6 GEMM TFLOPS (2*M*N*K / device time)"
 L2_FLUSH_BYTES = 256 << 20
-E2E_CHUNKS = 8  # row chunks of the end-to-end step (copies overlap the GEMM)
+E2E_ROW_CHUNKS = 8  # row chunks of A (and of D) in the end-to-end step
+CUDA_MEMCPY_D2H = 2
 # DRAM bytes (read + write) per launch of the dominant kernel, from one ncu capture of this
 # bench's own command (profiles/gemm_mxfp6_sm100_pair_cfg2.md); None where not captured yet.
 NCU_TRAFFIC_BYTES = {"cfg2": 257_806_848 + 114_925_568}
@@ -121,6 +122,18 @@ class ClockSampler:
         names = [n for b, n in self.REASONS.items() if self.reasons & b and n != "gpu_idle"]
         return {"sm_mhz": statistics.median(self.samples) if self.samples else None,
                 "sm_max_mhz": self.max_mhz, "reasons": names, "samples": len(self.samples)}
+
+
+def cudart_memcpy2d_async():
+    """cudaMemcpy2DAsync from the CUDA runtime the library is linked against (one pitched copy
+    per D block; torch has no pitched host copy)."""
+    import ctypes
+
+    f = ctypes.CDLL("libcudart.so.12").cudaMemcpy2DAsync
+    f.argtypes = [ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_size_t,
+                  ctypes.c_size_t, ctypes.c_int, ctypes.c_void_p]
+    f.restype = ctypes.c_int
+    return f
 
 
 def dist_env():
@@ -376,56 +389,82 @@ def run_ours(args):
     h2d = sum(p.numel() * p.element_size() for p in pinned.values())
     d2h = Dh.numel() * Dh.element_size()
 
-    # The step's transfers and math overlap: B^T and its scales go up first, then A in row chunks
-    # on a copy stream; each chunk's GEMM (the public gemm() on that chunk's rows of A, its scale
-    # atoms and its rows of D) runs on the compute stream as soon as its rows have landed, and each
-    # D chunk goes back on a third stream as soon as it is computed. Every byte still crosses PCIe
-    # inside every step.
+    # The step's transfers and math overlap in a two-dimensional block pipeline. A is cut into
+    # row chunks and B^T into row chunks (column chunks of B and D). The chunks go up on a copy
+    # stream in the order B0, A0, B1, A1, ..., so that a first block of D is computable after two
+    # chunks. Each block D[i, j] is one call of the library's public entry on the compute stream
+    # as soon as A_i and B_j have landed: mxfp6_gemm_gather with one destination (D's row i*mc)
+    # writes the block straight into D (row stride N, first column j*nc). Each block goes back on a third stream,
+    # as a pitched copy, as soon as it is computed. Every byte still crosses PCIe inside every step.
     s_up = torch.cuda.Stream(dev)
     s_down = torch.cuda.Stream(dev)
-    chunks = E2E_CHUNKS if M % (128 * E2E_CHUNKS) == 0 else 1
-    mc = M // chunks
+    ra = E2E_ROW_CHUNKS if M % (128 * E2E_ROW_CHUNKS) == 0 else 1
+    rc = args.e2e_cols if args.e2e_cols > 0 and N % (128 * args.e2e_cols) == 0 else 1
+    mc, nc = M // ra, N // rc
     sa_chunk = (mc // 128) * (Kp // 128) * 512  # scale atoms are row-block major
-    wsb_c = lib.gemm_workspace_size(mc, N, Kp, ot)  # a chunk's own route may split K
+    sb_chunk = (nc // 128) * (Kp // 128) * 512
+    wsb_c = lib.gemm_workspace_size(mc, nc, Kp, ot)  # a block's own route may split K
     ws_c = torch.empty(max(wsb_c, 16), dtype=torch.uint8, device=dev)
+    order = []
+    for k in range(max(ra, rc)):
+        if k < rc:
+            order.append(("B", k))
+        if k < ra:
+            order.append(("A", k))
+    memcpy2d = cudart_memcpy2d_async()
+    esz = Dh.element_size()
 
     def e2e_step():
         ev_start = torch.cuda.Event()
         ev_start.record(stream)
         s_up.wait_event(ev_start)
+        have_a, have_b, blocks = [], [], []
         with torch.cuda.stream(s_up):
-            dB2.copy_(pinned["Bt"], non_blocking=True)
-            dsB2.copy_(pinned["sB"], non_blocking=True)
-            up = []
-            for c in range(chunks):
-                r0, r1 = c * mc, (c + 1) * mc
-                dA2[r0:r1].copy_(pinned["A"][r0:r1], non_blocking=True)
-                dsA2[c * sa_chunk:(c + 1) * sa_chunk].copy_(pinned["sA"][c * sa_chunk:(c + 1) * sa_chunk],
-                                                            non_blocking=True)
+            for kind_c, k in order:
+                if kind_c == "A":
+                    dA2[k * mc:(k + 1) * mc].copy_(pinned["A"][k * mc:(k + 1) * mc], non_blocking=True)
+                    dsA2[k * sa_chunk:(k + 1) * sa_chunk].copy_(pinned["sA"][k * sa_chunk:(k + 1) * sa_chunk],
+                                                                non_blocking=True)
+                else:
+                    dB2[k * nc:(k + 1) * nc].copy_(pinned["Bt"][k * nc:(k + 1) * nc], non_blocking=True)
+                    dsB2[k * sb_chunk:(k + 1) * sb_chunk].copy_(pinned["sB"][k * sb_chunk:(k + 1) * sb_chunk],
+                                                                non_blocking=True)
                 ev = torch.cuda.Event()
                 ev.record(s_up)
-                up.append(ev)
+                if kind_c == "A":
+                    blocks += [(k, j, ev) for j in have_b]
+                    have_a.append(k)
+                else:
+                    blocks += [(i, k, ev) for i in have_a]
+                    have_b.append(k)
         done = []
-        for c in range(chunks):
-            r0, r1 = c * mc, (c + 1) * mc
-            stream.wait_event(up[c])
-            lib.gemm(ot, mc, N, Kp, dA2[r0:r1], dB2, dsA2[c * sa_chunk:], dsB2, D[r0:r1], rb, rb,
-                     ws_c if wsb_c else None, wsb_c, stream=stream)
+        for i, j, ev in blocks:
+            stream.wait_event(ev)
+            lib.gemm_gather(ot, mc, nc, Kp, dA2[i * mc:], dB2[j * nc:], dsA2[i * sa_chunk:], dsB2[j * sb_chunk:],
+                            [D[i * mc:].data_ptr()], N, j * nc, rb, rb, ws_c if wsb_c else None, wsb_c,
+                            stream=stream)
             ev = torch.cuda.Event()
             ev.record(stream)
-            done.append(ev)
-        with torch.cuda.stream(s_down):
-            for c in range(chunks):
-                s_down.wait_event(done[c])
-                Dh[c * mc:(c + 1) * mc].copy_(D[c * mc:(c + 1) * mc], non_blocking=True)
+            done.append((i, j, ev))
+        for i, j, ev in done:
+            s_down.wait_event(ev)
+            off = (i * mc * N + j * nc) * esz
+            err = memcpy2d(Dh.data_ptr() + off, N * esz, D.data_ptr() + off, N * esz, nc * esz, mc,
+                           CUDA_MEMCPY_D2H, s_down.cuda_stream)
+            if err != 0:
+                raise RuntimeError(f"cudaMemcpy2DAsync failed: {err}")
         ev_end = torch.cuda.Event()
         ev_end.record(s_down)
         stream.wait_event(ev_end)
 
     e2e_steps = max(3, min(args.steps, 20))
+    D_dev = D.clone()  # the device-timed result, to compare the end-to-end output with
     for _ in range(2):
         e2e_step()
     torch.cuda.synchronize()
+    bits = torch.int32 if tdt == torch.float32 else torch.int16
+    e2e_same = float((Dh.to(dev).view(bits) == D_dev.view(bits)).float().mean().item())
+    del D_dev
     if world > 1:
         dist.barrier()
     e0 = torch.cuda.Event(enable_timing=True)
@@ -673,9 +712,11 @@ def run_ours(args):
                          "splitk_workspace_bytes": 2 * splits * M * N * 4 if splits > 1 else 0},
             "cpu_baseline": cpu,
             "e2e": {"value": e2e_value, "unit": "TFLOPS", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                    "ms_per_step": e2e_ms,
-                    "path": f"pinned host -> H2D (B^T, scales, then A in {chunks} row chunks) overlapped with "
-                            f"mxfp6_gemm_stream (C ABI) per row chunk, overlapped with D2H per row chunk"},
+                    "ms_per_step": e2e_ms, "bitwise_equal_to_device_run": e2e_same,
+                    "path": f"pinned host -> H2D in {ra} row chunks of A and {rc} of B^T (interleaved, with their "
+                            f"scales), overlapped with one C-ABI call (mxfp6_gemm_gather, one destination) per "
+                            f"{mc}x{nc} block of D as soon as its chunks land, overlapped with a pitched D2H "
+                            f"copy per block"},
             "gpu_launches": launches,
             "clocks": clk.summary(),
             "device_status": status,
@@ -708,6 +749,8 @@ def main():
     ap.add_argument("--with-compact", action="store_true",
                     help="also time the same GEMM with A in the reference's compact layout (loader warps)")
     ap.add_argument("--ref-seconds", type=float, default=10.0, help="target CPU seconds per reference sample")
+    ap.add_argument("--e2e-cols", type=int, default=4,
+                    help="column chunks of B and D in the end-to-end pipeline (1 = row chunks only)")
     ap.add_argument("--vs-cublas", action="store_true",
                     help="also time cuBLASLt's MXFP8 block-scaled GEMM on the same shape (interleaved "
                          "with this library's, then each sustained for about a second with clocks)")

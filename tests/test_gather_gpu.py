@@ -3,7 +3,7 @@
 
 On one GPU: two local destinations of pitch 2N, at column 0 or N, on every route and output
 type; each must hold exactly the plain GEMM's D in its column range and keep its poison
-elsewhere. On two GPUs (skipped with fewer): each rank writes its shard into its own and its
+elsewhere. A D assembled block by block from one-destination calls matches the oracle. On two GPUs (skipped with fewer): each rank writes its shard into its own and its
 peer's gathered output through a CUDA IPC mapping; both ranks must end with [D_0 | D_1]."""
 from __future__ import annotations
 
@@ -59,6 +59,36 @@ def test_two_local_destinations(lib, ot, M, N, K, col0_blocks):
         assert torch.equal(_bits(t[:, col0:col0 + N].contiguous()), _bits(routed))
         other = t[:, N:] if col0 == 0 else t[:, :N]
         assert bool((_bits(other.contiguous()) == poison).all())
+
+
+@pytest.mark.parametrize("ot", ["F16", "BF16"])
+def test_blocks_assembled_into_one_output(lib, oracle, ot):
+    """The end-to-end pipeline's building block: D assembled from row chunks of A and row chunks
+    of B^T (with their scale atoms), each block written by a one-destination gather call at its
+    column offset of D; every block holds the oracle's values (its own route may split K)."""
+    from gpu_helpers import DeviceOperands, check
+    from mxfp6_b200.synth import make_operands
+    M, N, K, ra, rc = 1024, 1024, 2048, 2, 4
+    ops = make_operands(M, N, K, kind="codes", seed=77, exp_range=(116, 128))
+    dev = DeviceOperands(ops)
+    o = lib.OutType[ot]
+    mc, nc = M // ra, N // rc
+    sa_chunk = (mc // 128) * (ops.Kp // 128) * 512
+    sb_chunk = (nc // 128) * (ops.Kp // 128) * 512
+    D = torch.empty((M, N), dtype=TORCH_OUT[int(o)], device="cuda")
+    _bits(D).fill_(0x5A5A)
+    wsb = lib.gemm_workspace_size(mc, nc, ops.Kp, o)
+    ws = torch.empty(max(wsb, 16), dtype=torch.uint8, device="cuda") if wsb else None
+    for i in range(ra):
+        for j in range(rc):
+            lib.gemm_gather(o, mc, nc, ops.Kp, dev.A[i * mc:], dev.Bt[j * nc:], dev.sA[i * sa_chunk:],
+                            dev.sB[j * sb_chunk:], [D[i * mc:].data_ptr()], N, j * nc, ops.row_bytes, ops.row_bytes,
+                            ws, wsb)
+            assert lib.last_error() == lib.OK, lib.last_error_string()
+    torch.cuda.synchronize()
+    assert lib.device_status() == 0
+    ref = oracle.gemm(ops.A, ops.sA, ops.Bt, ops.sB, ops.Kp)
+    check(D.cpu(), ref, o, oracle, label=f"blocks {ra}x{rc} {ot}")
 
 
 def _rank_main(rank, world, port, out_q):
