@@ -314,6 +314,33 @@ def run_vs_cublas(M, N, K, step, stream, flush, dev, rounds=6, burst=8, sustain_
     return out
 
 
+def time_import_leg(lib, N, K, rb, stream, dev, reps=20):
+    """Device import of B^T [N x K] laid out as the reference lays out weights (gfx950
+    preshuffle_B, K padded to a multiple of 192) into this library's rows of rb bytes. The import
+    is a byte permutation, so random bytes time it as well as real weights."""
+    import torch
+
+    kp_ref = (K + 191) // 192 * 192
+    ref_b = torch.randint(0, 256, ((N // 32) * (kp_ref // 64) * 1536,), dtype=torch.uint8, device=dev)
+    imp_b = torch.empty((N, rb), dtype=torch.uint8, device=dev)
+    for _ in range(3):
+        assert lib.import_ref_B_device(ref_b, N, kp_ref, imp_b, rb, stream=stream) == lib.OK
+    i0 = torch.cuda.Event(enable_timing=True)
+    i1 = torch.cuda.Event(enable_timing=True)
+    i0.record(stream)
+    for _ in range(reps):
+        lib.import_ref_B_device(ref_b, N, kp_ref, imp_b, rb, stream=stream)
+    i1.record(stream)
+    torch.cuda.synchronize()
+    ms = i0.elapsed_time(i1) / reps
+    nbytes = ref_b.numel() + imp_b.numel()
+    _, hbm_peak, basis = load_peaks()
+    return {"what": f"B^T [{N}x{K}] from the reference's preshuffle_B layout (Kp_ref={kp_ref}) to this "
+                    f"library's rows of {rb} bytes, on the device",
+            "ms": ms, "gbs": nbytes / (ms * 1e-3) / 1e9, "frac_hbm": nbytes / (ms * 1e-3) / 1e9 / hbm_peak,
+            "peak_basis": f"{basis} copy bandwidth {hbm_peak:.0f} GB/s", "bytes_per_launch": nbytes}
+
+
 def run_ours(args):
     import torch
     import torch.distributed as dist
@@ -391,8 +418,8 @@ def run_ours(args):
 
     # The step's transfers and math overlap in a two-dimensional block pipeline. A is cut into
     # row chunks and B^T into row chunks (column chunks of B and D). The chunks go up on a copy
-    # stream in the order B0, A0, B1, A1, ..., so that a first block of D is computable after two
-    # chunks. Each block D[i, j] is one call of the library's public entry on the compute stream
+    # stream in an order that keeps D blocks coming as early as possible (below); a first block
+    # of D is computable after two chunks. Each block D[i, j] is one call of the library's public entry on the compute stream
     # as soon as A_i and B_j have landed: mxfp6_gemm_gather with one destination (D's row i*mc)
     # writes the block straight into D (row stride N, first column j*nc). Each block goes back on a third stream,
     # as a pitched copy, as soon as it is computed. Every byte still crosses PCIe inside every step.
@@ -405,12 +432,18 @@ def run_ours(args):
     sb_chunk = (nc // 128) * (Kp // 128) * 512
     wsb_c = lib.gemm_workspace_size(mc, nc, Kp, ot)  # a block's own route may split K
     ws_c = torch.empty(max(wsb_c, 16), dtype=torch.uint8, device=dev)
-    order = []
-    for k in range(max(ra, rc)):
-        if k < rc:
-            order.append(("B", k))
-        if k < ra:
-            order.append(("A", k))
+    # Upload order: greedily the chunk that makes the most new D blocks computable per byte (an A
+    # chunk completes one block per B chunk already up, and the other way round), B first.
+    order, na, nb = [], 0, 0
+    bytes_a, bytes_b = mc * rb, nc * rb
+    while na < ra or nb < rc:
+        take_a = nb < rc and na < ra and nb * bytes_b > na * bytes_a if nb else False
+        if na < ra and (nb == rc or take_a):
+            order.append(("A", na))
+            na += 1
+        else:
+            order.append(("B", nb))
+            nb += 1
     memcpy2d = cudart_memcpy2d_async()
     esz = Dh.element_size()
 
@@ -482,7 +515,7 @@ def run_ours(args):
     e2e_value = flops_rank * world / (e2e_ms * 1e-3) / 1e12
 
     # ---- activation quantisation on the device (cfg5: the step before the FFN GEMM) ----
-    quant = None
+    quant, imp_leg = None, None
     if args.config == "cfg5" and rank == 0:
         xf = torch.randn((M, K), device=dev, dtype=torch.float32)
         qa = torch.empty((M, Kp * 3 // 4), dtype=torch.uint8, device=dev)
@@ -504,6 +537,8 @@ def run_ours(args):
                  "gbs": qbytes / (qms * 1e-3) / 1e9, "frac_hbm": qbytes / (qms * 1e-3) / 1e9 / hbm_peak_q,
                  "peak_basis": f"{hbm_basis} copy bandwidth {hbm_peak_q:.0f} GB/s"}
         del xf, qa, qs
+
+        imp_leg = time_import_leg(lib, N, K, rb, stream, dev)
 
     # ---- compact A (the reference's row stride 3K/4 with K % 128 != 0; loader-warp producer) ----
     compact = None
@@ -725,6 +760,8 @@ def run_ours(args):
             line["allgather"] = allgather
         if quant:
             line["quantize_device"] = quant
+        if imp_leg:
+            line["import_ref_B_device"] = imp_leg
         if compact:
             line["compact_a"] = compact
         if as_ref:
@@ -751,13 +788,23 @@ def main():
     ap.add_argument("--ref-seconds", type=float, default=10.0, help="target CPU seconds per reference sample")
     ap.add_argument("--e2e-cols", type=int, default=4,
                     help="column chunks of B and D in the end-to-end pipeline (1 = row chunks only)")
+    ap.add_argument("--import-only", action="store_true",
+                    help="only time the device import of the config's B from the reference's layout")
     ap.add_argument("--vs-cublas", action="store_true",
                     help="also time cuBLASLt's MXFP8 block-scaled GEMM on the same shape (interleaved "
                          "with this library's, then each sustained for about a second with clocks)")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3
-    if args.impl == "reference":
+    if args.import_only:
+        import torch
+
+        import mxfp6_b200 as lib
+        M, N, K = CONFIGS[args.config][:3]
+        rb = lib.kpad(K) * 3 // 4
+        dev = torch.device("cuda", 0)
+        print(json.dumps({"import_ref_B_device": time_import_leg(lib, N, K, rb, torch.cuda.current_stream(dev), dev)}))
+    elif args.impl == "reference":
         run_reference_arm(args)
     else:
         run_ours(args)

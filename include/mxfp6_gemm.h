@@ -212,6 +212,23 @@ int mxfp6_import_ref_B(const uint8_t* ref_bsh, int N, int Kp_ref, uint8_t* out, 
  * the reference's MPW/NPW for the route it tiled for, subs its K_TILE/64 (3). */
 int mxfp6_import_ref_scales(const uint8_t* ref_tiled, int dim, int Kp_ref, int group, int subs, uint8_t* raw_out);
 
+/* Device versions of the two imports (device pointers, asynchronous on `stream`, NULL = legacy),
+ * writing this library's layouts directly in one pass.
+ * mxfp6_import_ref_B_device: d_ref_bsh as for mxfp6_import_ref_B (16-byte aligned); d_out
+ * receives B^T rows [N][out_row_bytes] (8-byte aligned, out_row_bytes % 8 == 0): the first
+ * min(3*Kp_ref/4, out_row_bytes) bytes of each row from the reference buffer, the rest zeroed.
+ * Use out_row_bytes = 3*kpad(K)/4; packed bytes dropped when that is below 3*Kp_ref/4 hold the
+ * reference's zero K padding. */
+int mxfp6_import_ref_B_device(const void* d_ref_bsh, int N, int Kp_ref, void* d_out, int out_row_bytes,
+                              void* stream);
+
+/* mxfp6_import_ref_scales_device: d_ref_tiled as for mxfp6_import_ref_scales; d_out_tiled (4-byte
+ * aligned) receives mxfp6_tiled_scale_bytes(dim, Kp) bytes in this library's atom layout for
+ * Kp (% 128 == 0): blocks past Kp_ref/32 and rows past dim get the finite code 127, blocks past
+ * Kp/32 are dropped. */
+int mxfp6_import_ref_scales_device(const void* d_ref_tiled, int dim, int Kp_ref, int group, int subs,
+                                   void* d_out_tiled, int Kp, void* stream);
+
 /* Device version of mxfp6_repad_rows (device pointers, asynchronous on `stream`): turns an A
  * operand in the reference's compact layout (row stride 3*K/4 with K % 128 != 0, which the
  * tensor-memory accelerator cannot address) into rows of 3*kpad(K)/4 bytes in a caller buffer;

@@ -76,6 +76,10 @@ _quantize_dev = _fn("mxfp6_quantize_device", C.c_int,
                     [C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_int, C.c_void_p])
 _quantize_dev_p = _fn("mxfp6_quantize_device_padded", C.c_int,
                       [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_int, C.c_void_p])
+_imp_B_dev = _fn("mxfp6_import_ref_B_device", C.c_int,
+                 [C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_int, C.c_void_p])
+_imp_sc_dev = _fn("mxfp6_import_ref_scales_device", C.c_int,
+                  [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_int, C.c_void_p])
 _repad_dev = _fn("mxfp6_repad_rows_device", C.c_int,
                  [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_int, C.c_void_p])
 _dequantize = _fn("mxfp6_dequantize", None, [_u8p, _u8p, C.c_int, C.c_int, _f32p])
@@ -332,6 +336,25 @@ def import_ref_scales(ref_tiled: np.ndarray, dim: int, Kp_ref: int, group: int, 
     out = np.full((dim, Kp // 32), 127, np.uint8)
     out[:, :Kp_ref // 32] = raw
     return out
+
+
+def _stream_arg(stream) -> int:
+    if stream is None:
+        return 0
+    return stream.cuda_stream if hasattr(stream, "cuda_stream") else _addr(stream)
+
+
+def import_ref_B_device(d_ref_bsh, N: int, Kp_ref: int, d_out, out_row_bytes: int, stream=None) -> int:
+    """mxfp6_import_ref_B_device: reference preshuffle_B buffer (device) -> B^T rows of
+    out_row_bytes in d_out (device). Returns an mxfp6_status."""
+    return _imp_B_dev(_addr(d_ref_bsh), N, Kp_ref, _addr(d_out), out_row_bytes, _stream_arg(stream))
+
+
+def import_ref_scales_device(d_ref_tiled, dim: int, Kp_ref: int, group: int, subs: int, d_out_tiled, Kp: int,
+                             stream=None) -> int:
+    """mxfp6_import_ref_scales_device: reference tiled scales (device) -> this library's scale atoms
+    for Kp in d_out_tiled (device). Returns an mxfp6_status."""
+    return _imp_sc_dev(_addr(d_ref_tiled), dim, Kp_ref, group, subs, _addr(d_out_tiled), Kp, _stream_arg(stream))
 
 
 def repad_rows(src: np.ndarray, bytes_used: int, dst_row_bytes: int) -> np.ndarray:
