@@ -589,6 +589,8 @@ def run_ours(args):
     # ---- optional NCCL all-gather of the D shards (timed separately) ----
     allgather = None
     if world > 1 and not args.no_allgather:
+        step()  # D from the routed full-shard GEMM again (the end-to-end blocks route differently)
+        torch.cuda.synchronize()
         gathered = torch.empty((world,) + tuple(D.shape), dtype=tdt, device=dev)
         for _ in range(2):
             dist.all_gather_into_tensor(gathered, D)
