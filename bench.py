@@ -20,6 +20,8 @@ the K steps, maximised over ranks. Clocks are sampled through NVML during the ti
 Extra keys: "timing_as_reference" repeats the measurement with the reference's own convention
 (8 warm-ups, 20 back-to-back calls, best of 4, no flush); --vs-cublas adds "vs_cublas_mxfp8",
 cuBLASLt's block-scaled MXFP8 GEMM on the same shape (burst, interleaved, and sustained).
+--config cfg5 adds the device quantiser and the device import of reference-layout weights;
+--import-only times just that import (a small command for ncu).
 
 --impl reference times the reference's own CPU GEMM (mxfp6_gemm_ref, compiled from its sources
 into oracle/_ref) on the host cores, on a bounded row sample of the same workload; rank 0 only.
