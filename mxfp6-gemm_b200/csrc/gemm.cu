@@ -91,35 +91,111 @@ EncodeTiledFn encode_fn() {
     return fn;
 }
 
+// Tensor maps depend only on their encode arguments, so each host thread keeps its last few:
+// a caller that repeats a call (same buffers, same shape) skips the driver's encode. The key holds
+// every argument that varies; the rest of each encode is fixed per map kind.
+struct TmapKey {
+    int kind;  // 0: FP6 operand, 1: scale atoms
+    int v[4];
+    const void* ptr;
+    bool operator==(const TmapKey& o) const {
+        return kind == o.kind && ptr == o.ptr && v[0] == o.v[0] && v[1] == o.v[1] && v[2] == o.v[2] &&
+               v[3] == o.v[3];
+    }
+};
+struct TmapCache {
+    static constexpr int kEntries = 16;
+    TmapKey key[kEntries];
+    CUtensorMap map[kEntries];
+    int used = 0, next = 0;
+    const CUtensorMap* find(const TmapKey& k) const {
+        for (int i = 0; i < used; i++)
+            if (key[i] == k) return &map[i];
+        return nullptr;
+    }
+    void put(const TmapKey& k, const CUtensorMap& m) {
+        key[next] = k;
+        map[next] = m;
+        next = (next + 1) % kEntries;
+        if (used < kEntries) used++;
+    }
+};
+thread_local TmapCache t_tmaps;
+thread_local int t_encode_status;  // CUresult of this thread's last failed encode (-1: no driver entry)
+
+// Driver calls (tensor-map encodes, address-range queries) need a current context. The runtime
+// binds its primary context to a host thread lazily, so a thread whose first CUDA work is such a
+// call (its streams and buffers made elsewhere) has none yet: bind the current device's primary
+// context and retry once.
+template <typename F>
+CUresult driver_call_in_context(F&& call) {
+    CUresult r = call();
+    if (r == CUDA_ERROR_INVALID_CONTEXT) {
+        int dev = 0;
+        if (cudaGetDevice(&dev) == cudaSuccess && cudaSetDevice(dev) == cudaSuccess) r = call();
+    }
+    return r;
+}
+
 // Packed FP6 matrix [rows][Kp] with row_bytes stride, read in 128 (K) x box_rows boxes through
 // the 16U6 unpack mode with 128-byte swizzle.
 bool make_fp6_tmap(CUtensorMap* map, const void* ptr, int rows, int Kp, int row_bytes, int box_rows) {
+    const TmapKey k{0, {rows, Kp, row_bytes, box_rows}, ptr};
+    if (const CUtensorMap* hit = t_tmaps.find(k)) {
+        *map = *hit;
+        return true;
+    }
     EncodeTiledFn fn = encode_fn();
-    if (!fn) return false;
+    if (!fn) {
+        t_encode_status = -1;
+        return false;
+    }
     cuuint64_t dims[2] = {(cuuint64_t)Kp, (cuuint64_t)rows};
     cuuint64_t strides[1] = {(cuuint64_t)row_bytes};
     cuuint32_t box[2] = {128u, (cuuint32_t)box_rows};
     cuuint32_t estr[2] = {1u, 1u};
-    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_16U6_ALIGN16B, 2, const_cast<void*>(ptr), dims,
-                    strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    return r == CUDA_SUCCESS;
+    const CUresult r = driver_call_in_context([&] {
+        return fn(map, CU_TENSOR_MAP_DATA_TYPE_16U6_ALIGN16B, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    });
+    if (r != CUDA_SUCCESS) {
+        t_encode_status = (int)r;
+        return false;
+    }
+    t_tmaps.put(k, *map);
+    return true;
 }
 
 // Tiled scales viewed as [row_atoms][k_slabs][128 x u32] (512-byte atoms), read one or two
 // atoms at a time; atoms past the last row block read as zero.
 bool make_sf_tmap(CUtensorMap* map, const void* ptr, int rows, int Kp, int box_atoms, int box_slabs = 1) {
+    const TmapKey k{1, {rows, Kp, box_atoms, box_slabs}, ptr};
+    if (const CUtensorMap* hit = t_tmaps.find(k)) {
+        *map = *hit;
+        return true;
+    }
     EncodeTiledFn fn = encode_fn();
-    if (!fn) return false;
+    if (!fn) {
+        t_encode_status = -1;
+        return false;
+    }
     const int k_slabs = Kp / 128, atoms = (rows + 127) / 128;
     cuuint64_t dims[3] = {128u, (cuuint64_t)k_slabs, (cuuint64_t)atoms};
     cuuint64_t strides[2] = {512u, (cuuint64_t)k_slabs * 512u};
     cuuint32_t box[3] = {128u, (cuuint32_t)box_slabs, (cuuint32_t)box_atoms};
     cuuint32_t estr[3] = {1u, 1u, 1u};
-    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT32, 3, const_cast<void*>(ptr), dims, strides, box, estr,
-                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    return r == CUDA_SUCCESS;
+    const CUresult r = driver_call_in_context([&] {
+        return fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT32, 3, const_cast<void*>(ptr), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    });
+    if (r != CUDA_SUCCESS) {
+        t_encode_status = (int)r;
+        return false;
+    }
+    t_tmaps.put(k, *map);
+    return true;
 }
 
 // ---- validation -----------------------------------------------------------------------------------
@@ -242,7 +318,8 @@ bool launch_gemm(int M, int N, int Kp, const void* dA, const void* dB, const uin
     CUtensorMap tmA, tmB;
     if (!make_a_tmap(AMODE, &tmA, dA, M, Kp, A_row_bytes, kern::BM) ||
         !make_fp6_tmap(&tmB, dB, N, Kp, B_row_bytes, BN)) {
-        set_error(MXFP6_ERR_CUDA, "cuTensorMapEncodeTiled failed for %dx%dx%d", M, N, Kp);
+        set_error(MXFP6_ERR_CUDA, "cuTensorMapEncodeTiled failed for %dx%dx%d (status %d)", M, N, Kp,
+                  t_encode_status);
         return false;
     }
     kern::Params p;
@@ -294,7 +371,8 @@ bool launch_pair(int M, int N, int Kp, const void* dA, const void* dB, const uin
     CUtensorMap tmA, tmB, tmSA, tmSB;
     if (!make_a_tmap(AMODE, &tmA, dA, M, Kp, A_row_bytes, 128) || !make_fp6_tmap(&tmB, dB, N, Kp, B_row_bytes, 128) ||
         !make_sf_tmap(&tmSA, sA, M, Kp, 1, C::SUB) || !make_sf_tmap(&tmSB, sB, N, Kp, 2, C::SUB)) {
-        set_error(MXFP6_ERR_CUDA, "cuTensorMapEncodeTiled failed for %dx%dx%d", M, N, Kp);
+        set_error(MXFP6_ERR_CUDA, "cuTensorMapEncodeTiled failed for %dx%dx%d (status %d)", M, N, Kp,
+                  t_encode_status);
         return false;
     }
     kern::Params p;
@@ -660,7 +738,9 @@ int mxfp6_ipc_export(const void* dptr, void* handle_out, size_t* offset_out) {
     if (!dptr || !handle_out || !offset_out || !range) return MXFP6_ERR_NULL_POINTER;
     CUdeviceptr base = 0;
     size_t size = 0;
-    if (range(&base, &size, reinterpret_cast<CUdeviceptr>(dptr)) != CUDA_SUCCESS) return MXFP6_ERR_CUDA;
+    if (driver_call_in_context([&] { return range(&base, &size, reinterpret_cast<CUdeviceptr>(dptr)); }) !=
+        CUDA_SUCCESS)
+        return MXFP6_ERR_CUDA;
     cudaIpcMemHandle_t h;
     if (cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base)) != cudaSuccess) return MXFP6_ERR_CUDA;
     std::memcpy(handle_out, &h, sizeof(h));
