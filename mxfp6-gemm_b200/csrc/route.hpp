@@ -13,7 +13,8 @@
 //   units   = ceil(M/MT) * ceil(N/NT) * S              work items handed out round-robin
 //   waves   = ceil(units / (sms / ctas_per_unit))      persistent CTAs (or pairs) take units
 //   time    = waves * (ceil(slabs / S) * T_slab + T_tile)   one slab = 128-deep K step
-//           + (2S + 1) * M*N*4 / HBM  when S > 1        partial write + reduce read + D write
+//           + T_fixed                                      the kernel's start-up beyond the smallest
+//           + T_reduce + (2S + 1) * M*N*4 / HBM  when S > 1   reduce launch, partial write + read, D
 //
 // T_slab is the time one SM (or pair) spends per slab: 256x256 and 128x256 tiles do the same
 // MMA work per SM per slab; their constants reflect how well each keeps the tensor pipe fed
@@ -36,19 +37,28 @@ inline size_t splitk_bytes(int M, int N, int splits) {
 
 inline double route_cost_us(int M, int N, int Kp, int MT, int NT, int S, int sms) {
     const double HBM = 6.5e6;  // bytes per us
-    double t_slab, t_tile;
+    // Fixed cost of a launch beyond the 128x128 kernel's, and of the split-K reduce's own launch,
+    // in the model's units. Measured back to back on small shapes, where they dominate: 128x128
+    // takes 6-8 us per call, 128x256 about 0.5 us more, the CTA pair about 4 us more, and a split
+    // about 5 us more. On those shapes the slab terms read about 1.7x short, so the fixed terms
+    // are scaled down by the same factor to keep the two comparable.
+    const double T_REDUCE_LAUNCH = 3.0;
+    double t_slab, t_tile, t_fixed;
     int per_unit;
     if (MT == 256) {
         t_slab = 0.30;  // us per 128-deep slab of a 256x256 pair tile (4 MMAs of 128x256 per SM)
         t_tile = 0.3;
+        t_fixed = 2.5;
         per_unit = 2;
     } else if (NT == 256) {
         t_slab = 0.40;
         t_tile = 1.0;
+        t_fixed = 0.3;
         per_unit = 1;
     } else {
         t_slab = 0.24;
         t_tile = 0.6;
+        t_fixed = 0.0;
         per_unit = 1;
     }
     const long long units = (long long)((M + MT - 1) / MT) * ((N + NT - 1) / NT) * S;
@@ -56,8 +66,8 @@ inline double route_cost_us(int M, int N, int Kp, int MT, int NT, int S, int sms
     const long long waves = (units + slots - 1) / slots;
     const int slabs = Kp / 128;
     const int per = (slabs + S - 1) / S;
-    double t = (double)waves * (per * t_slab + t_tile);
-    if (S > 1) t += (2.0 * S + 1.0) * (double)M * N * 4.0 / HBM;
+    double t = (double)waves * (per * t_slab + t_tile) + t_fixed;
+    if (S > 1) t += T_REDUCE_LAUNCH + (2.0 * S + 1.0) * (double)M * N * 4.0 / HBM;
     return t;
 }
 
