@@ -127,6 +127,18 @@ def test_route_examples(lib):
     assert lib.gemm_workspace_size(256, 256, 512) == 0
     assert lib.gemm_workspace_size(128, 128, 128) == 0
     assert lib.choose_tile(8192, 8192, 8192).MT == 256  # CTA-pair tile on machine-filling shapes
+    for shape in [(2048, 1024, 105728), (2048, 6144, 16128), (4096, 28672, 8192), (4096, 3584, 8192)]:
+        assert lib.choose_tile(*shape).MT == 256, shape
+
+
+@pytest.mark.parametrize("M,N,K", [(128, 128, 128), (256, 256, 512), (512, 512, 1024), (512, 256, 2048),
+                                   (1024, 2048, 8192)])
+def test_small_shapes_take_the_single_cta_kernel_unsplit(lib, M, N, K):
+    """Where a launch's fixed cost dominates, the route avoids the CTA pair's start-up and the
+    split-K reduce's extra launch (both measured slower on these shapes)."""
+    t = lib.choose_tile(M, N, K)
+    assert (t.MT, t.NT) == (128, 128)
+    assert lib.gemm_workspace_size(M, N, K) == 0
 
 
 def test_workspace_query_per_output_type(lib):
