@@ -62,6 +62,28 @@ def test_two_local_destinations(lib, ot, M, N, K, col0_blocks):
         assert bool((_bits(other.contiguous()) == poison).all())
 
 
+@pytest.mark.parametrize("M,N,K", [(512, 768, 1408), (2048, 2048, 2048), (1024, 512, 24576)])
+def test_eight_local_destinations(lib, M, N, K):
+    """The largest destination list (8): every destination holds exactly the plain GEMM's D, on
+    the single-CTA, pair and split routes (the regrouping epilogue and the reduce pass)."""
+    from gpu_helpers import DeviceOperands, run_gemm
+    from mxfp6_b200.synth import make_operands
+    ops = make_operands(M, N, K, kind="codes", seed=M + 3 * N + K)
+    dev = DeviceOperands(ops)
+    o = lib.OutType.BF16
+    routed = run_gemm(dev, o)
+    outs = [torch.full((M, N), 7.0, dtype=torch.bfloat16, device="cuda") for _ in range(8)]
+    wsb = lib.gemm_workspace_size(M, N, ops.Kp, o)
+    ws = torch.empty(max(wsb, 16), dtype=torch.uint8, device="cuda") if wsb else None
+    lib.gemm_gather(o, M, N, ops.Kp, dev.A, dev.Bt, dev.sA, dev.sB, outs, N, 0, ops.row_bytes, ops.row_bytes,
+                    ws, wsb)
+    assert lib.last_error() == lib.OK, lib.last_error_string()
+    torch.cuda.synchronize()
+    assert lib.device_status() == 0
+    for t in outs:
+        assert torch.equal(_bits(t.cpu()), _bits(routed))
+
+
 @pytest.mark.parametrize("ot", ["F16", "BF16"])
 def test_blocks_assembled_into_one_output(lib, oracle, ot):
     """The end-to-end pipeline's building block: D assembled from row chunks of A and row chunks
