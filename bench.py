@@ -358,6 +358,14 @@ def run_ours(args):
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
 
     M, N, K, kind, er, out_name = CONFIGS[args.config]
+    # --strong: the config's N is the job's total, split over the ranks (strong scaling);
+    # --shard-of G: run on this GPU the shard one rank of a G-GPU strong-scaled job holds.
+    shards = world if args.strong else args.shard_of
+    if shards > 1:
+        if N % (128 * shards):
+            raise SystemExit(f"N={N} does not split into {shards} shards of whole 128-column blocks")
+        N //= shards
+    n_total = N * shards if shards > 1 else N * world
     ot = lib.OutType[out_name]
     kw = {"exp_range": er} if er else {}
     # A is replicated (same seed everywhere); B^T's shard differs per rank (column-parallel).
@@ -726,18 +734,20 @@ def run_ours(args):
     peak = 2.0 * bf16_peak
     kernel_ms = min(per)  # dominant kernel: the GEMM (plus the split-K reduce when routed)
     achieved = flops_rank / (ms * 1e-3) / 1e12
-    route = lib.choose_tile(M, N, Kp)
-    splits = max(1, wsb // (M * N * 4))
+    route = lib.route(ot, M, N, Kp)  # tile and K splits
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": "TFLOPS", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "strong" if args.strong else "weak",
             "vs_baseline": None, "dtype": "fp6_e2m3 x fp6_e2m3 -> f32 accumulate",
             "data": "synthetic (seeded E2M3 codes uniform over 64 codes, E8M0 exponents per BASELINE)",
             "config": {"workload": CONFIG_DESC[args.config] + (f", N-sharded over {world} GPUs (per-GPU shard N={N})"
-                                                               if world > 1 else ""),
-                       "M": M, "N_per_gpu": N, "N_total": N * world, "K": K, "out": out_name,
-                       "route": {"MT": route.MT, "NT": route.NT, "splits": splits},
+                                                               if world > 1 else "")
+                       + (f", the shard of one GPU out of {shards} (N={N} of {n_total})"
+                          if world == 1 and shards > 1 else ""),
+                       "M": M, "N_per_gpu": N, "N_total": n_total, "K": K, "out": out_name,
+                       "route": route,
                        "parallelism": f"N-sharded x{world}, no collective on the GEMM path",
                        "l2": "256 MiB buffer written before every timed step (L2 flushed)"},
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
@@ -748,7 +758,7 @@ def run_ours(args):
                          "best_step_ms": kernel_ms,
                          "frac_of_nominal_fp6_dense": achieved / NOMINAL_FP6_TFLOPS,
                          "algorithmic_gbs": algo_bytes / (ms * 1e-3) / 1e9,
-                         "splitk_workspace_bytes": 2 * splits * M * N * 4 if splits > 1 else 0},
+                         "splitk_workspace_bytes": 2 * wsb},  # partials written, then read by the reduce
             "cpu_baseline": cpu,
             "e2e": {"value": e2e_value, "unit": "TFLOPS", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "ms_per_step": e2e_ms, "bitwise_equal_to_device_run": e2e_same,
@@ -792,6 +802,10 @@ def main():
     ap.add_argument("--ref-seconds", type=float, default=10.0, help="target CPU seconds per reference sample")
     ap.add_argument("--e2e-cols", type=int, default=4,
                     help="column chunks of B and D in the end-to-end pipeline (1 = row chunks only)")
+    ap.add_argument("--strong", action="store_true",
+                    help="split the config's N over the ranks (strong scaling) instead of N per rank")
+    ap.add_argument("--shard-of", type=int, default=1,
+                    help="on one GPU, run the N shard one rank of this many holds (strong scaling)")
     ap.add_argument("--import-only", action="store_true",
                     help="only time the device import of the config's B from the reference's layout")
     ap.add_argument("--vs-cublas", action="store_true",

@@ -107,6 +107,10 @@ int mxfp6_ipc_close(void* base);
 /* Route for (M,N,Kp): writes MT, NT, MPW, NPW into out[0..3]. */
 void mxfp6_choose_tile(int M, int N, int Kp, int* out4);
 
+/* The route gemm() takes for output type ot (no counterpart in the reference): writes MT, NT
+ * and the number of K splits into out[0..2]. FP32 output may split where FP16/BF16 does not. */
+void mxfp6_route(int ot, int M, int N, int Kp, int* out3);
+
 /* K granule (128) and K padded to it. */
 int mxfp6_k_tile(void);
 int mxfp6_kpad(int K);

@@ -632,6 +632,14 @@ void mxfp6_choose_tile(int M, int N, int Kp, int* out4) {
     }
 }
 
+void mxfp6_route(int ot, int M, int N, int Kp, int* out3) {
+    if (!out3) return;
+    const Route r = route_for_out(ot, M, N, Kp);
+    out3[0] = r.MT;
+    out3[1] = r.NT;
+    out3[2] = r.splits;
+}
+
 int mxfp6_k_tile(void) {
     return K_TILE;
 }

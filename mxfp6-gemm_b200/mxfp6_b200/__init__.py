@@ -65,6 +65,7 @@ _ws = _fn("mxfp6_gemm_workspace_size", C.c_size_t, [C.c_int, C.c_int, C.c_int])
 _ws_out = _fn("mxfp6_gemm_workspace_size_out", C.c_size_t, [C.c_int, C.c_int, C.c_int, C.c_int])
 _ws_a = _fn("mxfp6_gemm_workspace_size_a", C.c_size_t, [C.c_int, C.c_int, C.c_int, C.c_int])
 _choose = _fn("mxfp6_choose_tile", None, [C.c_int, C.c_int, C.c_int, C.POINTER(C.c_int)])
+_route = _fn("mxfp6_route", None, [C.c_int, C.c_int, C.c_int, C.c_int, C.POINTER(C.c_int)])
 _k_tile = _fn("mxfp6_k_tile", C.c_int, [])
 _kpad = _fn("mxfp6_kpad", C.c_int, [C.c_int])
 last_error = _fn("mxfp6_last_error", C.c_int, [])
@@ -134,6 +135,13 @@ def choose_tile(M: int, N: int, Kp: int) -> TileChoice:
     out = (C.c_int * 4)()
     _choose(M, N, Kp, out)
     return TileChoice(*out)
+
+
+def route(ot, M: int, N: int, Kp: int) -> dict:
+    """The route gemm() takes for output type ot: tile and K splits (mxfp6_route)."""
+    out = (C.c_int * 3)()
+    _route(int(ot), M, N, Kp, out)
+    return {"MT": out[0], "NT": out[1], "splits": out[2]}
 
 
 def gemm_workspace_size(M: int, N: int, Kp: int, ot=None) -> int:

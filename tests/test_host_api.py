@@ -113,9 +113,15 @@ def test_route_covers_every_shape(lib):
                 assert M % 128 == 0 and N % 128 == 0  # every tile covers the rest by masking
                 assert (t.MPW, t.NPW) == (t.MT // 32, t.NT // 32)
                 ws = lib.gemm_workspace_size(M, N, Kp)
-                assert ws % (M * N * 4) == 0
-                S = ws // (M * N * 4)
-                assert S == 0 or 2 <= S <= Kp // 128
+                need = 0
+                for ot in (lib.OutType.F16, lib.OutType.F32):
+                    r = lib.route(ot, M, N, Kp)
+                    if ot == lib.OutType.F16:  # choose_tile reports the FP16/BF16 route
+                        assert r["MT"] == t.MT and r["NT"] == t.NT
+                    assert 1 <= r["splits"] <= Kp // 128
+                    if r["splits"] > 1:
+                        need = max(need, r["splits"] * M * N * 4)
+                assert ws == need
 
 
 def test_route_examples(lib):
