@@ -95,7 +95,7 @@ EncodeTiledFn encode_fn() {
 // a caller that repeats a call (same buffers, same shape) skips the driver's encode. The key holds
 // every argument that varies; the rest of each encode is fixed per map kind.
 struct TmapKey {
-    int kind;  // 0: FP6 operand, 1: scale atoms
+    int kind;  // 0: FP6 operand, 1: scale atoms, 2: scale atoms read four times (pair B)
     int v[4];
     const void* ptr;
     bool operator==(const TmapKey& o) const {
@@ -187,6 +187,39 @@ bool make_sf_tmap(CUtensorMap* map, const void* ptr, int rows, int Kp, int box_a
     cuuint32_t estr[3] = {1u, 1u, 1u};
     const CUresult r = driver_call_in_context([&] {
         return fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT32, 3, const_cast<void*>(ptr), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    });
+    if (r != CUDA_SUCCESS) {
+        t_encode_status = (int)r;
+        return false;
+    }
+    t_tmaps.put(k, *map);
+    return true;
+}
+
+// B's scale atoms for the pair kernel, each read four times: a repeat dimension of stride 0 after
+// the atom's 128 words, so one box lands as atom 0 four times then atom 1 four times. That is
+// the source layout of one tcgen05.cp.128x256b, which fills all four lane quarters of the
+// accumulator's tensor memory with the same 256 columns' scales.
+bool make_sf_tmap_x4(CUtensorMap* map, const void* ptr, int rows, int Kp) {
+    const TmapKey k{2, {rows, Kp, 0, 0}, ptr};
+    if (const CUtensorMap* hit = t_tmaps.find(k)) {
+        *map = *hit;
+        return true;
+    }
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) {
+        t_encode_status = -1;
+        return false;
+    }
+    const int k_slabs = Kp / 128, atoms = (rows + 127) / 128;
+    cuuint64_t dims[4] = {128u, 4u, (cuuint64_t)k_slabs, (cuuint64_t)atoms};
+    cuuint64_t strides[3] = {0u, 512u, (cuuint64_t)k_slabs * 512u};
+    cuuint32_t box[4] = {128u, 4u, 1u, 2u};
+    cuuint32_t estr[4] = {1u, 1u, 1u, 1u};
+    const CUresult r = driver_call_in_context([&] {
+        return fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, const_cast<void*>(ptr), dims, strides, box, estr,
                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     });
@@ -370,7 +403,7 @@ bool launch_pair(int M, int N, int Kp, const void* dA, const void* dB, const uin
     }
     CUtensorMap tmA, tmB, tmSA, tmSB;
     if (!make_a_tmap(AMODE, &tmA, dA, M, Kp, A_row_bytes, 128) || !make_fp6_tmap(&tmB, dB, N, Kp, B_row_bytes, 128) ||
-        !make_sf_tmap(&tmSA, sA, M, Kp, 1, C::SUB) || !make_sf_tmap(&tmSB, sB, N, Kp, 2, C::SUB)) {
+        !make_sf_tmap(&tmSA, sA, M, Kp, 1, C::SUB) || !make_sf_tmap_x4(&tmSB, sB, N, Kp)) {
         set_error(MXFP6_ERR_CUDA, "cuTensorMapEncodeTiled failed for %dx%dx%d (status %d)", M, N, Kp,
                   t_encode_status);
         return false;

@@ -4,15 +4,19 @@
 //
 // Same math as gemm_mxfp6_sm100 (gemm_kernel.cuh); the pair layout halves what each SM stages:
 //   * CTA r of the pair loads A rows [m0 + 128r, +128) and B^T rows [n0 + 128r, +128) of every
-//     128-deep K slab (16U6 unpack, 128-byte swizzle), its own A scale atom and both B scale
-//     atoms (tensor loads with zero fill past the edges), into a 6-stage ring; all loads of both
-//     CTAs report to the leader's (rank 0) full barrier.
-//   * The leader's MMA thread copies the scale atoms into each CTA's tensor memory and issues
-//     tcgen05.mma.cta_group::2 (M = 256, N = 256, K = 32) four times per slab; each CTA's tensor
-//     memory receives its 128 rows x 256 FP32 columns. tcgen05.commit multicasts slot releases
-//     and "accumulator ready" to both CTAs.
+//     128-deep K slab (16U6 unpack, 128-byte swizzle), its own A scale atom, and both B scale
+//     atoms four times over (one tensor load through a zero-stride repeat dimension), with zero
+//     fill past the edges, into a 5-stage ring; all loads of both CTAs report to the leader's
+//     (rank 0) full barrier.
+//   * The leader's MMA thread copies the scales into each CTA's tensor memory, two copies per
+//     slab: A's atom with the broadcasting 32x128b.warpx4 copy, and B's 256 rows with one
+//     128x256b copy from the fourfold-staged atoms. B's scales are needed in all four lane
+//     quarters. One wide copy instead of two broadcast copies made the kernel 4-5% faster.
+//     It then issues tcgen05.mma.cta_group::2 (M = 256, N = 256, K = 32) four times per slab;
+//     each CTA's tensor memory receives its 128 rows x 256 FP32 columns. tcgen05.commit
+//     multicasts slot releases and "accumulator ready" to both CTAs.
 //   * Two accumulators share tensor memory with a 32-column overlap: buffer 0 = columns [0,256),
-//     buffer 1 = [224,480), scales at [480,492). The epilogue reads buffer 0 from its top chunk
+//     buffer 1 = [224,480); B scales at [480,488), A scales at [488,492). The epilogue reads buffer 0 from its top chunk
 //     down and buffer 1 from its bottom chunk up, so the overlap chunk is read first and the
 //     next tile's MMAs may start as soon as that one chunk has left tensor memory; the rest of
 //     the epilogue runs under the next tile's main loop.
@@ -26,11 +30,6 @@
 // Every wait is bounded (see gemm_kernel.cuh); a timeout also raises the peer's abort flag.
 #include "gemm_kernel.cuh"
 
-// 128-deep K slabs per pipeline stage (1 or 2).
-#ifndef MXFP6_PAIR_SUB
-#define MXFP6_PAIR_SUB 1
-#endif
-
 namespace mxfp6 {
 namespace kern {
 
@@ -38,23 +37,26 @@ template <int AMODE = A_TMA>
 struct PairConfig {
     static constexpr int BM = 256;  // rows per pair tile (128 per CTA)
     static constexpr int BN = 256;  // columns per pair tile (B rows 128 per CTA)
-    static constexpr int SUB = MXFP6_PAIR_SUB;           // 128-deep slabs per stage
-    static constexpr int STAGES = SUB == 1 ? 6 : 3;
+    static constexpr int SUB = 1;                        // 128-deep slabs per stage
+    static constexpr int STAGES = 5;
     static constexpr int SLAB_BYTES = 128 * BK;          // one 128-row x 128-K box in shared memory
     static constexpr int A_BYTES = SUB * SLAB_BYTES;
     static constexpr int B_BYTES = SUB * SLAB_BYTES;
     static constexpr int AB_STAGE = A_BYTES + B_BYTES;
-    static constexpr int SFA_BYTES = SUB * 512;          // own A atom per slab
-    static constexpr int SF_STAGE = SFA_BYTES + SUB * 1024;  // then both B atoms per slab
+    static constexpr int SFA_BYTES = 512;                // own A atom
+    // B's two atoms, each four times over (atom 0 x4, then atom 1 x4): the source of one
+    // 128x256b tensor-memory copy, which fills all four lane quarters without broadcasting.
+    static constexpr int SFB_BYTES = 4 * 1024;
+    static constexpr int SF_STAGE = SFA_BYTES + SFB_BYTES;
     static constexpr uint32_t SLAB_TX = 2 * (128 * BK * 3 / 4);  // packed A + B bytes per CTA
     static constexpr uint32_t tx_stage(int nsub) {                // leader's barrier counts both CTAs
         return 2 * (nsub * SLAB_TX + SF_STAGE);
     }
     static constexpr int TMEM_COLS = 512;
     static constexpr int BUF1_COL = 224;  // buffer 1 starts 32 columns below buffer 0's end
-    static constexpr int TMEM_SF = 480;  // per slab of a stage: A scales (4 columns), B scales (8)
-    static constexpr int SF_SET_COLS = 12;
-    static_assert(TMEM_SF + SUB * SF_SET_COLS <= 512, "tensor memory budget");
+    static constexpr int TMEM_SFB = 480;  // B scales: 8 columns (8-column aligned for the wide copy)
+    static constexpr int TMEM_SFA = 488;  // A scales: 4 columns
+    static_assert(TMEM_SFA + 4 <= 512, "tensor memory budget");
     static constexpr int EPI_WARPS = 4;
     static constexpr int BAR_BYTES = 256;
     static constexpr int SMEM_BYTES = 1024 + STAGES * (AB_STAGE + SF_STAGE) + BAR_BYTES + EPI_STG_BYTES;
@@ -176,10 +178,10 @@ __global__ void __launch_bounds__(threads_for(AMODE), 1)
                         sm100::tma_load_2d_pair(a_dst + C::A_BYTES + j * C::SLAB_BYTES, &tmB, fb, (kb + j) * BK,
                                                 b_row);
                     }
-                    // scale boxes are SUB slabs deep; a slab past the end reads as zero
+                    // scale atoms past the last row block read as zero
                     const uint32_t sf_dst = sf_base + stage * C::SF_STAGE;
                     sm100::tma_load_3d_pair(sf_dst, &tmSA, fb, 0, kb, tc.mb * 2 + (int)rank);
-                    sm100::tma_load_3d_pair(sf_dst + C::SFA_BYTES, &tmSB, fb, 0, kb, tc.nb * 2);
+                    sm100::tma_load_4d_pair(sf_dst + C::SFA_BYTES, &tmSB, fb, 0, 0, kb, tc.nb * 2);
                     issued_mask |= 1u << stage;
                     issued_phase = (issued_phase & ~(1u << stage)) | (phase << stage);
                     if (++stage == C::STAGES) {
@@ -241,16 +243,12 @@ __global__ void __launch_bounds__(threads_for(AMODE), 1)
                     }
                     const int nsub = tc.kb_count - i < C::SUB ? tc.kb_count - i : C::SUB;
                     const uint32_t sf_src = sf_base + stage * C::SF_STAGE;
-                    for (int j = 0; j < nsub; j++) {  // scale atoms of slab j -> scale set j
-                        const uint32_t sfa_t = tmem_base + C::TMEM_SF + C::SF_SET_COLS * j;
-                        sm100::tc_cp_32x128b_warpx4_pair(sfa_t, sm100::make_sf_desc(sf_src + 512 * j));
-                        sm100::tc_cp_32x128b_warpx4_pair(sfa_t + 4, sm100::make_sf_desc(sf_src + C::SFA_BYTES + 512 * j));
-                        sm100::tc_cp_32x128b_warpx4_pair(sfa_t + 8, sm100::make_sf_desc(sf_src + C::SFA_BYTES +
-                                                                                        512 * (C::SUB + j)));
-                    }
+                    // A's atom: one broadcast copy; B's two atoms, staged four times over: one wide copy
+                    sm100::tc_cp_32x128b_warpx4_pair(tmem_base + C::TMEM_SFA, sm100::make_sf_desc(sf_src));
+                    sm100::tc_cp_128x256b_pair(tmem_base + C::TMEM_SFB, sm100::make_sf_wide_desc(sf_src + C::SFA_BYTES));
                     for (int j = 0; j < nsub; j++) {
-                        const uint32_t sfa_t = tmem_base + C::TMEM_SF + C::SF_SET_COLS * j;
-                        const uint32_t sfb_t = sfa_t + 4;
+                        const uint32_t sfa_t = tmem_base + C::TMEM_SFA;
+                        const uint32_t sfb_t = tmem_base + C::TMEM_SFB;
                         const uint32_t off16 = (uint32_t)(stage * C::AB_STAGE + j * C::SLAB_BYTES) >> 4;
 #pragma unroll
                         for (int k = 0; k < BK / 32; k++) {

@@ -181,6 +181,13 @@ __device__ __forceinline__ uint64_t make_sf_desc(uint32_t saddr) {
     return make_smem_desc(saddr, 0, 128, 0);
 }
 
+// Source for tcgen05.cp.128x256b: 128 rows of 32 bytes as two 16-byte columns, no swizzle. Column
+// h (2048 bytes apart) holds rows 0..127 of 16 bytes each, 8-row groups 128 bytes apart; with
+// scale atom h staged four times over, row i reads that atom's row i % 32.
+__device__ __forceinline__ uint64_t make_sf_wide_desc(uint32_t saddr) {
+    return make_smem_desc(saddr, 2048, 128, 0);
+}
+
 // Copy one 32-row x 128-bit scale chunk from shared memory into tensor memory columns
 // [taddr, taddr+4), replicated into all four 32-lane quarters.
 __device__ __forceinline__ void tc_cp_32x128b_warpx4(uint32_t taddr, uint64_t sdesc) {
@@ -284,6 +291,15 @@ __device__ __forceinline__ void tma_load_3d_pair(uint32_t dst, const void* tmap,
         : "memory");
 }
 
+__device__ __forceinline__ void tma_load_4d_pair(uint32_t dst, const void* tmap, uint32_t bar, int c0, int c1,
+                                                 int c2, int c3) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(dst),
+        "l"(tmap), "r"(bar), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+        : "memory");
+}
+
 __device__ __forceinline__ void tmem_alloc_pair(uint32_t dst_smem, uint32_t ncols) {
     asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem), "r"(ncols)
                  : "memory");
@@ -298,6 +314,12 @@ __device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols
 // Each CTA of the pair copies its own shared-memory scale chunk into its own tensor memory.
 __device__ __forceinline__ void tc_cp_32x128b_warpx4_pair(uint32_t taddr, uint64_t sdesc) {
     asm volatile("tcgen05.cp.cta_group::2.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
+}
+
+// 128 rows x 256 bits from shared memory into tensor memory columns [taddr, taddr+8): row i lands in
+// lane i, no broadcast. taddr's column is a multiple of 8.
+__device__ __forceinline__ void tc_cp_128x256b_pair(uint32_t taddr, uint64_t sdesc) {
+    asm volatile("tcgen05.cp.cta_group::2.128x256b [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
 }
 
 __device__ __forceinline__ void tc_mma_mxf8f6f4_pair(uint32_t d_taddr, uint64_t adesc, uint64_t bdesc,
