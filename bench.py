@@ -62,7 +62,7 @@ E2E_ROW_CHUNKS = 8  # row chunks of A (and of D) in the end-to-end step
 CUDA_MEMCPY_D2H = 2
 # DRAM bytes (read + write) per launch of the dominant kernel, from one ncu capture of this
 # bench's own command (profiles/gemm_mxfp6_sm100_pair_cfg2.md); None where not captured yet.
-NCU_TRAFFIC_BYTES = {"cfg2": 167_113_472 + 113_330_688}
+NCU_TRAFFIC_BYTES = {"cfg2": 163_303_936 + 112_370_944}
 NOMINAL_FP6_TFLOPS = 4500.0  # B200 dense FP8/FP6 tensor rate, nominal (no sparsity)
 
 
