@@ -126,6 +126,22 @@ class ClockSampler:
                 "sm_max_mhz": self.max_mhz, "reasons": names, "samples": len(self.samples)}
 
 
+def e2e_upload_order(n_a, n_b, bytes_a, bytes_b):
+    """Order of the end-to-end step's uploads: B chunk 0 first, then A while fewer A bytes than B
+    bytes are up (B on a tie), so that the computable D blocks (one per pair of an A chunk and a
+    B chunk already up) grow about as fast as possible per byte sent."""
+    order, na, nb = [], 0, 0
+    while na < n_a or nb < n_b:
+        take_a = nb > 0 and na < n_a and (nb == n_b or nb * bytes_b > na * bytes_a)
+        if take_a:
+            order.append(("A", na))
+            na += 1
+        else:
+            order.append(("B", nb))
+            nb += 1
+    return order
+
+
 def cudart_memcpy2d_async():
     """cudaMemcpy2DAsync from the CUDA runtime the library is linked against (one pitched copy
     per D block; torch has no pitched host copy)."""
@@ -442,18 +458,7 @@ def run_ours(args):
     sb_chunk = (nc // 128) * (Kp // 128) * 512
     wsb_c = lib.gemm_workspace_size(mc, nc, Kp, ot)  # a block's own route may split K
     ws_c = torch.empty(max(wsb_c, 16), dtype=torch.uint8, device=dev)
-    # Upload order: greedily the chunk that makes the most new D blocks computable per byte (an A
-    # chunk completes one block per B chunk already up, and the other way round), B first.
-    order, na, nb = [], 0, 0
-    bytes_a, bytes_b = mc * rb, nc * rb
-    while na < ra or nb < rc:
-        take_a = nb < rc and na < ra and nb * bytes_b > na * bytes_a if nb else False
-        if na < ra and (nb == rc or take_a):
-            order.append(("A", na))
-            na += 1
-        else:
-            order.append(("B", nb))
-            nb += 1
+    order = e2e_upload_order(ra, rc, mc * rb, nc * rb)
     memcpy2d = cudart_memcpy2d_async()
     esz = Dh.element_size()
 
