@@ -8,9 +8,17 @@ Workload (a "step" = one D = A·B call over one batch of synthetic operands):
         exponents uniform in [118, 136] (seeded; no dataset).
   N>1   the same per-GPU shape, N-sharded (column-parallel): the job is D[8192, 8192*N] =
         A[8192, 8192] · B[8192, 8192*N] with A replicated and B / D split by columns, so per-GPU
-        work is fixed (weak scaling) and no collective sits on the GEMM path. The optional NCCL
-        all-gather of D is timed separately ("allgather").
+        work is fixed (weak scaling) and no collective sits on the GEMM path.
 Other configs (--config cfg1..cfg5) run the same harness on BASELINE's other shapes.
+
+Every line also carries
+  "strong"      BASELINE config 5 (the FFN up-projection 4096 x 28672 x 8192, BF16 out) with B and
+                D split column-parallel over the N ranks: total and per-GPU TFLOPS, the same
+                GEMM unsplit on one GPU, the efficiency against it, whether the shard results
+                equal the unsplit D bit for bit, and the optional D all-gather (NCCL, and the
+                fused epilogue gather over NVLink peer stores) at N>1;
+  "per_config"  (N=1) device-timed TFLOPS, route and roofline fractions of BASELINE configs 1, 3,
+                4 and 5, plus the device quantiser and the reference-layout import on config 5.
 
 Timing: W untimed warm-up steps; then exactly K steps between a barrier + synchronize on each
 side; before every timed step a 256 MiB buffer is written to flush the 126 MB L2, and each
@@ -19,12 +27,13 @@ the K steps, maximised over ranks. Clocks are sampled through NVML during the ti
 
 Extra keys: "timing_as_reference" repeats the measurement with the reference's own convention
 (8 warm-ups, 20 back-to-back calls, best of 4, no flush); --vs-cublas adds "vs_cublas_mxfp8",
-cuBLASLt's block-scaled MXFP8 GEMM on the same shape (burst, interleaved, and sustained).
---config cfg5 adds the device quantiser and the device import of reference-layout weights;
---import-only times just that import (a small command for ncu).
+cuBLASLt's block-scaled MXFP8 GEMM on the same shape (burst, interleaved, and sustained);
+--import-only times just the device import of reference-layout weights (a small command for ncu).
 
 --impl reference times the reference's own CPU GEMM (mxfp6_gemm_ref, compiled from its sources
-into oracle/_ref) on the host cores, on a bounded row sample of the same workload; rank 0 only.
+into oracle/_ref) on the host cores, on a bounded row sample of the same workload and the same
+operands; rank 0 only. That arm loads no part of this library: its operands come from the numpy
+generator below (and, for config 5, the reference's own quantiser).
 """
 from __future__ import annotations
 
@@ -39,7 +48,7 @@ import time
 import numpy as np
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
-sys.path.insert(0, os.path.join(ROOT, "mxfp6-gemm_b200"))
+PKG_DIR = os.path.join(ROOT, "mxfp6-gemm_b200")
 
 CONFIGS = {
     # name: (M, N, K, kind, exp_range, out)
@@ -56,14 +65,21 @@ CONFIG_DESC = {
     "cfg4": "MXFP6 GEMM M=2048 N=6144 K=16128, BF16 output",
     "cfg5": "LLM FFN up-projection MXFP6 GEMM M=4096 N=28672 K=8192, BF16 output",
 }
+CFG5_SIGMA = (1.0, 0.02)  # A activation-like N(0, 1), B weight-like N(0, 0.02)
 METRIC = "MXFP6 GEMM TFLOPS (2*M*N*K / device time)"
 L2_FLUSH_BYTES = 256 << 20
+L2_NOTE = "256 MiB buffer written before every timed step (L2 flushed)"
 E2E_ROW_CHUNKS = 8  # row chunks of A (and of D) in the end-to-end step
 CUDA_MEMCPY_D2H = 2
 # DRAM bytes (read + write) per launch of the dominant kernel, from one ncu capture of this
 # bench's own command (profiles/gemm_mxfp6_sm100_pair_cfg2.md); None where not captured yet.
 NCU_TRAFFIC_BYTES = {"cfg2": 163_303_936 + 112_370_944}
 NOMINAL_FP6_TFLOPS = 4500.0  # B200 dense FP8/FP6 tensor rate, nominal (no sparsity)
+SEED_A, SEED_B = 1000, 2000  # operand seeds (B: plus the rank of its shard)
+
+
+def kpad(K: int) -> int:
+    return (K + 127) // 128 * 128
 
 
 def load_peaks():
@@ -161,6 +177,50 @@ def dist_env():
     return rank, world, local
 
 
+# ---- synthetic operands (numpy; shared by both arms) ----------------------------------------------
+
+def synth_codes(M, N, K, seed, exp_range):
+    """Seeded E2M3 codes uniform over all 64 codes (the packed bytes are then uniform random
+    bytes) and E8M0 exponents uniform in exp_range, in this library's host layouts: A packed
+    [M][3Kp/4], B^T packed [N][3Kp/4], raw scales [rows][Kp/32]; a K tail past K is zero codes.
+    Draw order A, B^T, sA, sB from one generator (the same draws as the package's
+    synth.make_operands(kind="codes"), which the parity tests use)."""
+    Kp = kpad(K)
+    rb = Kp * 3 // 4
+    rng = np.random.default_rng(seed)
+    A = rng.integers(0, 256, (M, rb), dtype=np.uint8)
+    Bt = rng.integers(0, 256, (N, rb), dtype=np.uint8)
+    lo, hi = exp_range
+    sA = rng.integers(lo, hi + 1, (M, Kp // 32), dtype=np.uint8)
+    sB = rng.integers(lo, hi + 1, (N, Kp // 32), dtype=np.uint8)
+    if K < Kp:
+        A[:, K * 3 // 4:] = 0
+        Bt[:, K * 3 // 4:] = 0
+    return A, sA, Bt, sB
+
+
+def synth_normal_rows(rows, K, seed, sigma, quantize):
+    """rows x K floats ~ N(0, sigma), quantised per 32-block with max-abs E8M0 scaling by
+    `quantize` (the reference's quantize_to_mxfp6, or this library's bit-identical one)."""
+    rng = np.random.default_rng(seed)
+    x = rng.standard_normal((rows, K), dtype=np.float32) * np.float32(sigma)
+    return quantize(x)
+
+
+def bench_config(cfg_name, world, shards):
+    """The `config` object of a line; both arms print the same one for the same arguments."""
+    M, N, K, _, _, out = CONFIGS[cfg_name]
+    n_per = N // shards if shards > 1 else N
+    n_total = n_per * shards if shards > 1 else n_per * world
+    workload = CONFIG_DESC[cfg_name]
+    if world > 1:
+        workload += f", N-sharded over {world} GPUs (per-GPU shard N={n_per})"
+    if world == 1 and shards > 1:
+        workload += f", the shard of one GPU out of {shards} (N={n_per} of {n_total})"
+    return {"workload": workload, "M": M, "N_per_gpu": n_per, "N_total": n_total, "K": K, "out": out,
+            "parallelism": f"N-sharded x{world}, no collective on the GEMM path", "l2": L2_NOTE}
+
+
 # ---- reference arm: the reference's CPU GEMM on the host cores ------------------------------------
 
 def _cpu_threads(N, K):
@@ -178,35 +238,54 @@ def _cpu_threads(N, K):
 _CPU_OPS = {}
 
 
-def cpu_reference_sample(cfg_name, target_s=10.0, threads=None, rows_override=None):
+def _cpu_operands(cfg_name, n_cols):
+    """The GPU arm's operands for rank 0: A (seed SEED_A) and the first B^T shard (seed SEED_B),
+    with raw scales, from the numpy generator; config 5 is quantised by the reference's own
+    quantize_to_mxfp6 (oracle/_ref) or, where that is not built, the C restatement."""
+    key = (cfg_name, n_cols)
+    if key not in _CPU_OPS:
+        M, N, K, kind, er, _ = CONFIGS[cfg_name]
+        if kind == "codes":
+            A, sA, _, _ = synth_codes(M, 128, K, SEED_A, er)
+            _, _, Bt, sB = synth_codes(128, n_cols, K, SEED_B, er)
+        else:
+            sys.path.insert(0, os.path.join(ROOT, "oracle"))
+            from oracle import Oracle, Reference, reference_available
+            q = Reference().quantize if reference_available() else Oracle().quantize
+            A, sA = synth_normal_rows(M, K, SEED_A, CFG5_SIGMA[0], q)
+            Bt, sB = synth_normal_rows(n_cols, K, SEED_B, CFG5_SIGMA[1], q)
+        _CPU_OPS[key] = (A, sA, Bt, sB)
+    return _CPU_OPS[key]
+
+
+def cpu_reference_sample(cfg_name, n_cols=None, target_s=10.0, threads=None, rows_override=None):
     """Time mxfp6_gemm_ref (oracle/_ref, the reference's own CPU path; else the C restatement)
-    on a row sample of the config: `rows` rows of A against all of B, sized to about target_s."""
+    on a row sample of the config: `rows` rows of A against all n_cols columns of B, sized to
+    about target_s."""
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     from oracle import Oracle, Reference, reference_available
-    from mxfp6_b200.synth import make_operands
 
-    M, N, K, kind, er, _ = CONFIGS[cfg_name]
-    threads = threads or _cpu_threads(N, K)
-    kw = {"exp_range": er} if er else {}
-    if cfg_name not in _CPU_OPS:  # same distributions as the GPU run
-        _CPU_OPS[cfg_name] = make_operands(M, N, K, kind=kind, seed=2026, **kw)
-    ops = _CPU_OPS[cfg_name]
-    if reference_available() and ops.Kp == K:
+    M, N, K, _, _, _ = CONFIGS[cfg_name]
+    n_cols = n_cols or N
+    threads = threads or _cpu_threads(n_cols, K)
+    A, sA, Bt, sB = _cpu_operands(cfg_name, n_cols)
+    Kp = kpad(K)
+    if reference_available() and Kp == K:
         ref, kind_s = Reference(), "reference"
 
         def run(rows):
-            return ref.gemm(ops.A[:rows], ops.sA[:rows], ops.Bt, ops.sB, K, threads=threads)
+            return ref.gemm(A[:rows], sA[:rows], Bt, sB, K, threads=threads)
     else:
         o, kind_s = Oracle(), "port"
 
         def run(rows):
-            return o.gemm(ops.A[:rows], ops.sA[:rows], ops.Bt, ops.sB, ops.Kp, threads=threads)
+            return o.gemm(A[:rows], sA[:rows], Bt, sB, Kp, threads=threads)
 
     if rows_override is None:
         # A warm-up call, then two timed sizes separate the per-call cost (each call dequantises
         # all of B per thread) from the per-row cost, so the sample lands near target_s.
-        run(min(ops.M, threads))
-        r1, r2 = min(ops.M, 4 * threads), min(ops.M, 16 * threads)
+        run(min(M, threads))
+        r1, r2 = min(M, 4 * threads), min(M, 16 * threads)
         t0 = time.perf_counter()
         run(r1)
         t1 = time.perf_counter() - t0
@@ -216,15 +295,15 @@ def cpu_reference_sample(cfg_name, target_s=10.0, threads=None, rows_override=No
         per_row = (t2 - t1) / (r2 - r1) if r2 > r1 and t2 > t1 else t2 / max(r2, 1)
         fixed = max(0.0, t2 - per_row * r2)
         rows = int((target_s - fixed) / max(per_row, 1e-9))
-        rows = max(r2, min(ops.M, rows // threads * threads if rows >= threads else rows))
+        rows = max(r2, min(M, rows // threads * threads if rows >= threads else rows))
     else:
-        rows = min(rows_override, ops.M)
+        rows = min(rows_override, M)
     t0 = time.perf_counter()
     run(rows)
     dt = time.perf_counter() - t0
-    tflops = 2.0 * rows * N * K / dt / 1e12
-    sample = (f"{rows} of {M} rows of A x all {N} columns of B, K={K} "
-              f"({2.0 * rows * N * K / 1e9:.1f} GFLOP) in {dt:.2f} s on {threads} threads")
+    tflops = 2.0 * rows * n_cols * K / dt / 1e12
+    sample = (f"{rows} of {M} rows of A x all {n_cols} columns of B, K={K} "
+              f"({2.0 * rows * n_cols * K / 1e9:.1f} GFLOP) in {dt:.2f} s on {threads} threads")
     return tflops, kind_s, threads, sample, rows
 
 
@@ -232,28 +311,32 @@ def run_reference_arm(args):
     rank, world, _ = dist_env()
     if rank != 0:
         return
-    _, _, _, _, _, out = CONFIGS[args.config]
-    M, N, K = CONFIGS[args.config][:3]
-    threads = _cpu_threads(N, K)
+    shards = world if args.strong else args.shard_of
+    config = bench_config(args.config, world, shards)
+    n_cols, K = config["N_per_gpu"], config["K"]
+    threads = _cpu_threads(n_cols, K)
     # one calibration pass picks the row sample, then K timed steps of that sample
-    v0, kind_s, cores, sample, rows = cpu_reference_sample(args.config, target_s=min(args.ref_seconds, 150.0 / max(1, args.steps + args.warmup)),
-                                                           threads=threads)
+    _, kind_s, cores, sample, rows = cpu_reference_sample(
+        args.config, n_cols, target_s=min(args.ref_seconds, 150.0 / max(1, args.steps + args.warmup)),
+        threads=threads)
     for _ in range(max(0, min(args.warmup, 1) - 1)):
-        cpu_reference_sample(args.config, threads=threads, rows_override=rows)
+        cpu_reference_sample(args.config, n_cols, threads=threads, rows_override=rows)
     vals = []
     for _ in range(args.steps):
-        v, kind_s, cores, sample, _ = cpu_reference_sample(args.config, threads=threads, rows_override=rows)
+        v, kind_s, cores, sample, _ = cpu_reference_sample(args.config, n_cols, threads=threads,
+                                                           rows_override=rows)
         vals.append(v)
     value = statistics.mean(vals)
-    flops_step = 2.0 * rows * N * K
+    flops_step = 2.0 * rows * n_cols * K
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "TFLOPS", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": flops_step / (value * 1e12) * 1e3,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-        "data": "synthetic (seeded E2M3 codes / E8M0 scales, BASELINE distributions)",
-        "config": {"workload": CONFIG_DESC[args.config], "M": M, "N": N, "K": K, "out": out,
-                   "sample_rows": rows},
-        "cpu_baseline": {"value": value, "unit": "TFLOPS", "cores": cores, "kind": kind_s, "sample": sample},
+        "higher_is_better": True, "scaling": "strong" if args.strong else "weak", "vs_baseline": None,
+        "dtype": "fp6_e2m3 x fp6_e2m3 -> f32 accumulate",
+        "data": "synthetic (seeded E2M3 codes uniform over 64 codes, E8M0 exponents per BASELINE)",
+        "config": config,
+        "cpu_baseline": {"value": value, "unit": "TFLOPS", "cores": cores, "kind": kind_s,
+                         "sample": f"each step: {sample}"},
         "e2e": {"value": value, "unit": "TFLOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -359,12 +442,330 @@ def time_import_leg(lib, N, K, rb, stream, dev, reps=20):
             "peak_basis": f"{basis} copy bandwidth {hbm_peak:.0f} GB/s", "bytes_per_launch": nbytes}
 
 
+def _torch_out(lib, torch, ot):
+    return {lib.OutType.F32: torch.float32, lib.OutType.F16: torch.float16, lib.OutType.BF16: torch.bfloat16}[ot]
+
+
+def codes_device_operands(lib, torch, cfg_name, n_cols, b_seed, dev):
+    """A (seed SEED_A) and an n_cols-row B^T (seed b_seed) of a "codes" config on the device, scales
+    in the GEMM's atom layout."""
+    M, _, K, _, er, _ = CONFIGS[cfg_name]
+    A, sA, _, _ = synth_codes(M, 128, K, SEED_A, er)
+    _, _, Bt, sB = synth_codes(128, n_cols, K, b_seed, er)
+    Kp = kpad(K)
+    return (torch.from_numpy(A).to(dev), torch.from_numpy(lib.preprocess_scale(sA, M, Kp)).to(dev),
+            torch.from_numpy(Bt).to(dev), torch.from_numpy(lib.preprocess_scale(sB, n_cols, Kp)).to(dev))
+
+
+def cfg5_device_operands(lib, torch, dev, stream):
+    """BASELINE config 5 on the device: A ~ N(0, 1) [M][K] and B^T ~ N(0, 0.02) [N][K] from torch's
+    seeded generator, quantised per 32-block with max-abs E8M0 scaling by this library's device
+    quantiser (bit-identical to quantize_to_mxfp6), scales in the GEMM's atom layout."""
+    M, N, K, _, _, _ = CONFIGS["cfg5"]
+    Kp = kpad(K)
+    out = []
+    for rows, seed, sigma in ((M, SEED_A, CFG5_SIGMA[0]), (N, SEED_B, CFG5_SIGMA[1])):
+        g = torch.Generator(device=dev)
+        g.manual_seed(seed)
+        x = torch.randn((rows, K), generator=g, device=dev, dtype=torch.float32) * sigma
+        q = torch.empty((rows, Kp * 3 // 4), dtype=torch.uint8, device=dev)
+        s = torch.empty(lib.tiled_scale_bytes(rows, Kp), dtype=torch.uint8, device=dev)
+        rc = lib.quantize_device(x, rows, K, q, s, True, stream=stream)
+        if rc != lib.OK:
+            raise RuntimeError(f"device quantiser failed: {rc}")
+        del x
+        out += [q, s]
+    torch.cuda.synchronize()
+    return out  # A, sA, Bt, sB
+
+
+def workspace(lib, torch, M, N, Kp, ot, dev):
+    """Workspace for this output type's route (the type-free query is the max over types)."""
+    wsb = lib.gemm_workspace_size(M, N, Kp, ot)
+    return (torch.empty(wsb, dtype=torch.uint8, device=dev) if wsb else None), wsb
+
+
+def timed_calls(torch, fn, steps, warmup, flush, stream):
+    """Per-call device times (ms): `warmup` untimed calls, then `steps` calls, each after an L2
+    flush, between CUDA events on the launching stream."""
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    for i, (a, b) in enumerate(ev):
+        flush.fill_(i & 0xFF)
+        a.record(stream)
+        fn()
+        b.record(stream)
+    torch.cuda.synchronize()
+    return [a.elapsed_time(b) for a, b in ev]
+
+
+def roofline_fields(M, N, K, Kp, out_bytes, ms, wsb):
+    bf16_peak, _, basis = load_peaks()
+    peak = 2.0 * bf16_peak
+    tflops = 2.0 * M * N * K / (ms * 1e-3) / 1e12
+    algo_bytes = (M + N) * Kp * 3 // 4 + (M + N) * (Kp // 32) + M * N * out_bytes
+    return {"tflops": tflops, "frac": tflops / peak, "frac_of_nominal_fp6_dense": tflops / NOMINAL_FP6_TFLOPS,
+            "peak": peak, "peak_basis": f"2 x {basis} cuBLAS bf16 dense ({bf16_peak:.1f} TFLOP/s)",
+            "algorithmic_bytes": algo_bytes, "algorithmic_gbs": algo_bytes / (ms * 1e-3) / 1e9,
+            "splitk_workspace_bytes": 2 * wsb}
+
+
+def per_config_leg(lib, torch, dev, stream, flush, steps, warmup, skip):
+    """N=1: BASELINE configs 1, 3 and 4 timed like the headline (config 5 comes from the strong
+    leg, which at N=1 is config 5 on one GPU)."""
+    out = {}
+    for name in ("cfg1", "cfg3", "cfg4"):
+        if name == skip:
+            continue
+        M, N, K, _, _, out_name = CONFIGS[name]
+        Kp = kpad(K)
+        rb = Kp * 3 // 4
+        ot = lib.OutType[out_name]
+        A, sA, Bt, sB = codes_device_operands(lib, torch, name, N, SEED_B, dev)
+        D = torch.empty((M, N), dtype=_torch_out(lib, torch, ot), device=dev)
+        ws, wsb = workspace(lib, torch, M, N, Kp, ot, dev)
+
+        def call():
+            lib.gemm(ot, M, N, Kp, A, Bt, sA, sB, D, rb, rb, ws, wsb, stream=stream)
+
+        per = timed_calls(torch, call, steps, warmup, flush, stream)
+        err, status = lib.last_error(), lib.device_status()
+        ms = sum(per) / len(per)
+        entry = {"workload": CONFIG_DESC[name], "M": M, "N": N, "K": K, "out": out_name,
+                 "route": lib.route(ot, M, N, Kp), "ms": ms, "best_ms": min(per), "steps": steps,
+                 "error": err, "device_status": status}
+        entry.update(roofline_fields(M, N, K, Kp, D.element_size(), ms, wsb))
+        out[name] = entry
+        del A, sA, Bt, sB, D, ws
+    return out
+
+
+def device_legs_cfg5(lib, torch, dev, stream, A, Bt):
+    """The steps either side of the config-5 GEMM on the device: quantising the activations, and
+    importing weights held in the reference's (gfx950) preprocessed layout."""
+    M, N, K, _, _, _ = CONFIGS["cfg5"]
+    Kp = kpad(K)
+    rb = Kp * 3 // 4
+    _, hbm_peak, basis = load_peaks()
+    xf = torch.randn((M, K), device=dev, dtype=torch.float32)
+    qa = torch.empty((M, rb), dtype=torch.uint8, device=dev)
+    qs = torch.empty(lib.tiled_scale_bytes(M, Kp), dtype=torch.uint8, device=dev)
+    for _ in range(3):
+        assert lib.quantize_device(xf, M, K, qa, qs, True, stream=stream) == lib.OK
+    q0 = torch.cuda.Event(enable_timing=True)
+    q1 = torch.cuda.Event(enable_timing=True)
+    reps = 20
+    q0.record(stream)
+    for _ in range(reps):
+        lib.quantize_device(xf, M, K, qa, qs, True, stream=stream)
+    q1.record(stream)
+    torch.cuda.synchronize()
+    qms = q0.elapsed_time(q1) / reps
+    qbytes = M * K * 4 + M * K * 3 // 4 + M * K // 32
+    quant = {"what": f"quantize A [{M}x{K}] fp32 -> MXFP6 + tiled scales on the device", "ms": qms,
+             "gbs": qbytes / (qms * 1e-3) / 1e9, "frac_hbm": qbytes / (qms * 1e-3) / 1e9 / hbm_peak,
+             "peak_basis": f"{basis} copy bandwidth {hbm_peak:.0f} GB/s"}
+    del xf, qa, qs
+    return quant, time_import_leg(lib, N, K, rb, stream, dev)
+
+
+def gather_legs(lib, torch, dist, dev, stream, flush, rank, world, ot, tdt, M, Ng, Kp, rb, A, Bt_r, sA, sB_r,
+                D_r, ws, wsb, shard_ms, D_ref):
+    """The optional gather of the column shards into every rank's row-major D[M][world*Ng]:
+    NCCL all-gather of the finished shards, and the fused alternative (mxfp6_gemm_gather: the
+    GEMM's epilogue stores each D chunk into every rank's gathered D through CUDA IPC peer
+    pointers). Both are checked bit for bit against D_ref, the unsplit GEMM of this rank."""
+    from mxfp6_b200.shard import assemble_columns
+
+    bits = torch.int32 if tdt == torch.float32 else torch.int16
+    gathered = torch.empty((world, M, Ng), dtype=tdt, device=dev)
+    for _ in range(2):
+        dist.all_gather_into_tensor(gathered, D_r)
+    torch.cuda.synchronize()
+    dist.barrier()
+    g0 = torch.cuda.Event(enable_timing=True)
+    g1 = torch.cuda.Event(enable_timing=True)
+    reps = 5
+    g0.record(stream)
+    for _ in range(reps):
+        dist.all_gather_into_tensor(gathered, D_r)
+    g1.record(stream)
+    torch.cuda.synchronize()
+    t = torch.tensor([g0.elapsed_time(g1) / reps], device=dev, dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ag_ms = float(t.item())
+    nbytes = D_r.numel() * D_r.element_size()
+    same = torch.equal(assemble_columns(gathered).view(bits), D_ref.view(bits))
+    f = torch.tensor([1 if same else 0], device=dev, dtype=torch.int32)
+    dist.all_reduce(f, op=dist.ReduceOp.MIN)
+    out = {"nccl_allgather": {"ms": ag_ms, "bytes_per_rank": nbytes,
+                              "bus_gbs": nbytes * (world - 1) / (ag_ms * 1e-3) / 1e9,
+                              "gemm_then_allgather_ms": shard_ms + ag_ms,
+                              "assembled_equals_one_gpu_D": bool(f.item() == 1),
+                              "what": "NCCL all_gather_into_tensor of the [M][N/g] shards, reassembled row-major"}}
+    del gathered
+
+    fused = {"unavailable": "fused gather skipped"}
+    ok_local, handle = 1, (None, 0)
+    gathered2 = torch.empty((M, Ng * world), dtype=tdt, device=dev)
+    try:
+        handle = lib.ipc_export(gathered2)
+    except Exception as e:  # reported, and every rank skips together
+        ok_local, fused = 0, {"unavailable": f"ipc export: {e}"}
+    handles = [None] * world
+    dist.all_gather_object(handles, handle)
+    dsts, bases = [], []
+    for r in range(world):
+        if r == rank:
+            dsts.append(gathered2.data_ptr())
+        elif ok_local and handles[r][0] is not None:
+            try:
+                base, ptr = lib.ipc_import(*handles[r])
+                bases.append(base)
+                dsts.append(ptr)
+            except Exception as e:
+                ok_local, fused = 0, {"unavailable": f"ipc import: {e}"}
+        else:
+            ok_local = 0
+    flag = torch.tensor([ok_local], device=dev, dtype=torch.int32)
+    dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+    if int(flag.item()) == 1:
+        def fstep():
+            lib.gemm_gather(ot, M, Ng, Kp, A, Bt_r, sA, sB_r, dsts, Ng * world, rank * Ng, rb, rb, ws, wsb,
+                            stream=stream)
+
+        for _ in range(2):
+            fstep()
+        torch.cuda.synchronize()
+        fail = torch.tensor([0 if lib.last_error() == lib.OK else 1], device=dev, dtype=torch.int32)
+        dist.all_reduce(fail, op=dist.ReduceOp.MAX)
+        if int(fail.item()) == 0:
+            fts = []
+            for i in range(reps):
+                dist.barrier()
+                flush.fill_(i & 0xFF)
+                torch.cuda.synchronize()
+                f0 = torch.cuda.Event(enable_timing=True)
+                f1 = torch.cuda.Event(enable_timing=True)
+                f0.record(stream)
+                fstep()
+                f1.record(stream)
+                torch.cuda.synchronize()
+                fts.append(f0.elapsed_time(f1))
+            t = torch.tensor([sum(fts) / len(fts)], device=dev, dtype=torch.float64)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            f_ms = float(t.item())
+            dist.barrier()  # every rank's peer stores have landed
+            same = torch.equal(gathered2.view(bits), D_ref.view(bits))
+            sflag = torch.tensor([1 if same else 0], device=dev, dtype=torch.int32)
+            dist.all_reduce(sflag, op=dist.ReduceOp.MIN)
+            fused = {"ms": f_ms, "speedup_vs_gemm_then_allgather": (shard_ms + ag_ms) / f_ms,
+                     "nvlink_bytes_per_rank": nbytes * (world - 1),
+                     "equals_one_gpu_D": bool(sflag.item() == 1), "device_status": lib.device_status(),
+                     "what": "mxfp6_gemm_gather: the shard GEMM's epilogue stores each D chunk into all ranks' "
+                             "gathered [M][N] outputs through CUDA IPC peer pointers"}
+        else:
+            fused = {"unavailable": "mxfp6_gemm_gather rejected the call on some rank"}
+    torch.cuda.synchronize()
+    dist.barrier()
+    for base in bases:
+        lib.ipc_close(base)
+    dist.barrier()
+    out["fused_gather"] = fused
+    del gathered2
+    return out
+
+
+def strong_leg(lib, torch, dist, dev, stream, flush, rank, world, steps, warmup, with_gather, with_device_legs):
+    """BASELINE config 5 with B and D split column-parallel over the ranks (strong scaling): rank r
+    computes D[:, r*N/g : (r+1)*N/g] from all of A and its rows of B^T; no collective on the GEMM
+    path. Timed like the headline (flushed L2, events, max over ranks). Each rank also runs the
+    unsplit GEMM on its GPU, for the efficiency and as the reference its shard must equal bit for
+    bit."""
+    M, N, K, _, _, out_name = CONFIGS["cfg5"]
+    Kp = kpad(K)
+    rb = Kp * 3 // 4
+    ot = lib.OutType[out_name]
+    tdt = _torch_out(lib, torch, ot)
+    A, sA, Bt, sB = cfg5_device_operands(lib, torch, dev, stream)
+    Ng = N // world
+    atoms = Kp // 128 * 512  # scale bytes per 128 rows
+    Bt_r = Bt[rank * Ng:(rank + 1) * Ng]
+    sB_r = sB[rank * Ng // 128 * atoms:(rank + 1) * Ng // 128 * atoms]
+    D_r = torch.empty((M, Ng), dtype=tdt, device=dev)
+    ws_r, wsb_r = workspace(lib, torch, M, Ng, Kp, ot, dev)
+
+    def shard():
+        lib.gemm(ot, M, Ng, Kp, A, Bt_r, sA, sB_r, D_r, rb, rb, ws_r, wsb_r, stream=stream)
+
+    for _ in range(warmup):
+        shard()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(dev.index or 0) as clk:
+        per = timed_calls(torch, shard, steps, 0, flush, stream)
+    if world > 1:
+        dist.barrier()
+    ms_local = sum(per) / len(per)
+    err, status = lib.last_error(), lib.device_status()
+
+    def max_over_ranks(v):
+        if world == 1:
+            return v
+        t = torch.tensor([v], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    ms = max_over_ranks(ms_local)
+    total = 2.0 * M * N * K / (ms * 1e-3) / 1e12
+    entry = {"workload": CONFIG_DESC["cfg5"] + f", B and D split column-parallel over {world} GPU(s)",
+             "M": M, "N_total": N, "N_per_gpu": Ng, "K": K, "out": out_name, "route": lib.route(ot, M, Ng, Kp),
+             "ms": ms, "total_tflops": total, "per_gpu_tflops": total / world, "steps": steps,
+             "clocks": clk.summary(), "error": err, "device_status": status}
+    entry.update({k: v for k, v in roofline_fields(M, Ng, K, Kp, D_r.element_size(), ms, wsb_r).items()
+                  if k not in ("tflops",)})
+    if world == 1:
+        D_full = D_r
+        entry["one_gpu"] = {"ms": ms, "tflops": total}
+        entry["efficiency_vs_one_gpu"] = 1.0
+    else:
+        D_full = torch.empty((M, N), dtype=tdt, device=dev)
+        ws_f, wsb_f = workspace(lib, torch, M, N, Kp, ot, dev)
+
+        def full():
+            lib.gemm(ot, M, N, Kp, A, Bt, sA, sB, D_full, rb, rb, ws_f, wsb_f, stream=stream)
+
+        per_f = timed_calls(torch, full, steps, warmup, flush, stream)
+        ms_f = max_over_ranks(sum(per_f) / len(per_f))
+        tf1 = 2.0 * M * N * K / (ms_f * 1e-3) / 1e12
+        entry["one_gpu"] = {"ms": ms_f, "tflops": tf1, "route": lib.route(ot, M, N, Kp),
+                            "how": "the unsplit GEMM on each rank's GPU, max over ranks"}
+        entry["efficiency_vs_one_gpu"] = (total / world) / tf1
+        bits = torch.int32 if tdt == torch.float32 else torch.int16
+        same = torch.equal(D_r.view(bits), D_full[:, rank * Ng:(rank + 1) * Ng].contiguous().view(bits))
+        f = torch.tensor([1 if same else 0], device=dev, dtype=torch.int32)
+        dist.all_reduce(f, op=dist.ReduceOp.MIN)
+        entry["shards_equal_one_gpu_D"] = bool(f.item() == 1)
+        if with_gather:
+            entry.update(gather_legs(lib, torch, dist, dev, stream, flush, rank, world, ot, tdt, M, Ng, Kp, rb,
+                                     A, Bt_r, sA, sB_r, D_r, ws_r, wsb_r, ms, D_full))
+        del ws_f
+    if with_device_legs and world == 1:
+        entry["quantize_device"], entry["import_ref_B_device"] = device_legs_cfg5(lib, torch, dev, stream, A, Bt)
+    del A, sA, Bt, sB, D_r, D_full
+    return entry
+
+
 def run_ours(args):
+    sys.path.insert(0, PKG_DIR)
     import torch
     import torch.distributed as dist
 
     import mxfp6_b200 as lib
-    from mxfp6_b200.synth import make_operands
 
     rank, world, local = dist_env()
     torch.cuda.set_device(local)
@@ -377,31 +778,29 @@ def run_ours(args):
     # --strong: the config's N is the job's total, split over the ranks (strong scaling);
     # --shard-of G: run on this GPU the shard one rank of a G-GPU strong-scaled job holds.
     shards = world if args.strong else args.shard_of
-    if shards > 1:
-        if N % (128 * shards):
-            raise SystemExit(f"N={N} does not split into {shards} shards of whole 128-column blocks")
-        N //= shards
-    n_total = N * shards if shards > 1 else N * world
+    config = bench_config(args.config, world, shards)
+    N = config["N_per_gpu"]
     ot = lib.OutType[out_name]
-    kw = {"exp_range": er} if er else {}
-    # A is replicated (same seed everywhere); B^T's shard differs per rank (column-parallel).
-    a_ops = make_operands(M, 128, K, kind=kind, seed=1000, **kw)
-    b_ops = make_operands(128, N, K, kind=kind, seed=2000 + rank, **kw)
-    Kp = a_ops.Kp
+    Kp = kpad(K)
     rb = Kp * 3 // 4
-    A = torch.from_numpy(a_ops.A).to(dev)
-    Bt = torch.from_numpy(b_ops.Bt).to(dev)
-    sA = torch.from_numpy(lib.preprocess_scale(a_ops.sA, M, Kp)).to(dev)
-    sB = torch.from_numpy(lib.preprocess_scale(b_ops.sB, N, Kp)).to(dev)
-    tdt = {lib.OutType.F32: torch.float32, lib.OutType.F16: torch.float16, lib.OutType.BF16: torch.bfloat16}[ot]
-    D = torch.empty((M, N), dtype=tdt, device=dev)
-    wsb = lib.gemm_workspace_size(M, N, Kp, ot)  # this output type's split (the type-free query is the max)
-    ws = torch.empty(max(wsb, 16), dtype=torch.uint8, device=dev)
-    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
     stream = torch.cuda.current_stream(dev)
+    # A is replicated (same seed everywhere); B^T's shard differs per rank (column-parallel).
+    if kind == "codes":
+        A, sA, Bt, sB = codes_device_operands(lib, torch, args.config, N, SEED_B + rank, dev)
+    else:
+        A, sA, Bt_all, sB_all = cfg5_device_operands(lib, torch, dev, stream)
+        r0 = rank if args.strong else 0
+        atoms = Kp // 128 * 512
+        Bt = Bt_all[r0 * N:(r0 + 1) * N].clone()
+        sB = sB_all[r0 * N // 128 * atoms:(r0 + 1) * N // 128 * atoms].clone()
+        del Bt_all, sB_all
+    tdt = _torch_out(lib, torch, ot)
+    D = torch.empty((M, N), dtype=tdt, device=dev)
+    ws, wsb = workspace(lib, torch, M, N, Kp, ot, dev)
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
 
     def step():
-        lib.gemm(ot, M, N, Kp, A, Bt, sA, sB, D, rb, rb, ws if wsb else None, wsb, stream=stream)
+        lib.gemm(ot, M, N, Kp, A, Bt, sA, sB, D, rb, rb, ws, wsb, stream=stream)
 
     for _ in range(args.warmup):
         step()
@@ -444,11 +843,12 @@ def run_ours(args):
 
     # The step's transfers and math overlap in a two-dimensional block pipeline. A is cut into
     # row chunks and B^T into row chunks (column chunks of B and D). The chunks go up on a copy
-    # stream in an order that keeps D blocks coming as early as possible (below); a first block
-    # of D is computable after two chunks. Each block D[i, j] is one call of the library's public entry on the compute stream
-    # as soon as A_i and B_j have landed: mxfp6_gemm_gather with one destination (D's row i*mc)
-    # writes the block straight into D (row stride N, first column j*nc). Each block goes back on a third stream,
-    # as a pitched copy, as soon as it is computed. Every byte still crosses PCIe inside every step.
+    # stream in an order that keeps D blocks coming as early as possible (e2e_upload_order); a
+    # first block of D is computable after two chunks. Each block D[i, j] is one call of the
+    # library's public entry on the compute stream as soon as A_i and B_j have landed:
+    # mxfp6_gemm_gather with one destination (D's row i*mc) writes the block straight into D
+    # (row stride N, first column j*nc). Each block goes back on a third stream, as a pitched
+    # copy, as soon as it is computed. Every byte still crosses PCIe inside every step.
     s_up = torch.cuda.Stream(dev)
     s_down = torch.cuda.Stream(dev)
     ra = E2E_ROW_CHUNKS if M % (128 * E2E_ROW_CHUNKS) == 0 else 1
@@ -456,8 +856,7 @@ def run_ours(args):
     mc, nc = M // ra, N // rc
     sa_chunk = (mc // 128) * (Kp // 128) * 512  # scale atoms are row-block major
     sb_chunk = (nc // 128) * (Kp // 128) * 512
-    wsb_c = lib.gemm_workspace_size(mc, nc, Kp, ot)  # a block's own route may split K
-    ws_c = torch.empty(max(wsb_c, 16), dtype=torch.uint8, device=dev)
+    ws_c, wsb_c = workspace(lib, torch, mc, nc, Kp, ot, dev)  # a block's own route may split K
     order = e2e_upload_order(ra, rc, mc * rb, nc * rb)
     memcpy2d = cudart_memcpy2d_async()
     esz = Dh.element_size()
@@ -489,8 +888,7 @@ def run_ours(args):
         for i, j, ev in blocks:
             stream.wait_event(ev)
             lib.gemm_gather(ot, mc, nc, Kp, dA2[i * mc:], dB2[j * nc:], dsA2[i * sa_chunk:], dsB2[j * sb_chunk:],
-                            [D[i * mc:].data_ptr()], N, j * nc, rb, rb, ws_c if wsb_c else None, wsb_c,
-                            stream=stream)
+                            [D[i * mc:].data_ptr()], N, j * nc, rb, rb, ws_c, wsb_c, stream=stream)
             ev = torch.cuda.Event()
             ev.record(stream)
             done.append((i, j, ev))
@@ -528,32 +926,7 @@ def run_ours(args):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_ms = float(t.item())
     e2e_value = flops_rank * world / (e2e_ms * 1e-3) / 1e12
-
-    # ---- activation quantisation on the device (cfg5: the step before the FFN GEMM) ----
-    quant, imp_leg = None, None
-    if args.config == "cfg5" and rank == 0:
-        xf = torch.randn((M, K), device=dev, dtype=torch.float32)
-        qa = torch.empty((M, Kp * 3 // 4), dtype=torch.uint8, device=dev)
-        qs = torch.empty(lib.tiled_scale_bytes(M, Kp), dtype=torch.uint8, device=dev)
-        for _ in range(3):
-            assert lib.quantize_device(xf, M, K, qa, qs, True, stream=stream) == lib.OK
-        q0 = torch.cuda.Event(enable_timing=True)
-        q1 = torch.cuda.Event(enable_timing=True)
-        reps = 20
-        q0.record(stream)
-        for _ in range(reps):
-            lib.quantize_device(xf, M, K, qa, qs, True, stream=stream)
-        q1.record(stream)
-        torch.cuda.synchronize()
-        qms = q0.elapsed_time(q1) / reps
-        qbytes = M * K * 4 + M * K * 3 // 4 + M * K // 32
-        _, hbm_peak_q, hbm_basis = load_peaks()
-        quant = {"what": f"quantize A [{M}x{K}] fp32 -> MXFP6 + tiled scales on the device", "ms": qms,
-                 "gbs": qbytes / (qms * 1e-3) / 1e9, "frac_hbm": qbytes / (qms * 1e-3) / 1e9 / hbm_peak_q,
-                 "peak_basis": f"{hbm_basis} copy bandwidth {hbm_peak_q:.0f} GB/s"}
-        del xf, qa, qs
-
-        imp_leg = time_import_leg(lib, N, K, rb, stream, dev)
+    del pinned, dA2, dB2, dsA2, dsB2, Dh, ws_c
 
     # ---- compact A (the reference's row stride 3K/4 with K % 128 != 0; loader-warp producer) ----
     compact = None
@@ -563,32 +936,19 @@ def run_ours(args):
         Ac = A[:, :rbc].contiguous()
         Btc = Bt.clone()
         Btc[:, rbc:] = 0  # the recipe's zero B tail
-        for _ in range(3):
-            lib.gemm(ot, M, N, Kp, Ac, Btc, sA, sB, D, rbc, rb, ws if wsb else None, wsb, stream=stream)
-        torch.cuda.synchronize()
+
+        def cstep(w, wb):
+            lib.gemm(ot, M, N, Kp, Ac, Btc, sA, sB, D, rbc, rb, w, wb, stream=stream)
+
+        cper = timed_calls(torch, lambda: cstep(ws, wsb), 10, 3, flush, stream)
         assert lib.last_error() == lib.OK, lib.last_error_string()
-        cs = [torch.cuda.Event(enable_timing=True) for _ in range(20)]
-        for i in range(10):
-            flush.fill_(i & 0xFF)
-            cs[2 * i].record(stream)
-            lib.gemm(ot, M, N, Kp, Ac, Btc, sA, sB, D, rbc, rb, ws if wsb else None, wsb, stream=stream)
-            cs[2 * i + 1].record(stream)
-        torch.cuda.synchronize()
-        cms = sum(cs[2 * i].elapsed_time(cs[2 * i + 1]) for i in range(10)) / 10
+        cms = sum(cper) / len(cper)
         # with a workspace sized for this A: re-pad into the workspace, then the tensor load
         wsa = lib.gemm_workspace_size_a(M, N, Kp, rbc)
         wsa_t = torch.empty(wsa, dtype=torch.uint8, device=dev)
-        for _ in range(3):
-            lib.gemm(ot, M, N, Kp, Ac, Btc, sA, sB, D, rbc, rb, wsa_t, wsa, stream=stream)
-        torch.cuda.synchronize()
+        rper = timed_calls(torch, lambda: cstep(wsa_t, wsa), 10, 3, flush, stream)
         assert lib.last_error() == lib.OK, lib.last_error_string()
-        for i in range(10):
-            flush.fill_(i & 0xFF)
-            cs[2 * i].record(stream)
-            lib.gemm(ot, M, N, Kp, Ac, Btc, sA, sB, D, rbc, rb, wsa_t, wsa, stream=stream)
-            cs[2 * i + 1].record(stream)
-        torch.cuda.synchronize()
-        rms = sum(cs[2 * i].elapsed_time(cs[2 * i + 1]) for i in range(10)) / 10
+        rms = sum(rper) / len(rper)
         compact = {"what": f"same GEMM with A in the reference's compact layout (K={Kc}, A_row_bytes={rbc}, "
                            f"not a multiple of 32)",
                    "in_place": {"how": "workspace from the reference's query: loader-warp cp.async producer",
@@ -600,110 +960,6 @@ def run_ours(args):
                              "time_ratio_vs_tensor_load": ms / rms},
                    "device_status": lib.device_status()}
         del Ac, Btc, wsa_t
-
-    # ---- optional NCCL all-gather of the D shards (timed separately) ----
-    allgather = None
-    if world > 1 and not args.no_allgather:
-        step()  # D from the routed full-shard GEMM again (the end-to-end blocks route differently)
-        torch.cuda.synchronize()
-        gathered = torch.empty((world,) + tuple(D.shape), dtype=tdt, device=dev)
-        for _ in range(2):
-            dist.all_gather_into_tensor(gathered, D)
-        torch.cuda.synchronize()
-        dist.barrier()
-        g0 = torch.cuda.Event(enable_timing=True)
-        g1 = torch.cuda.Event(enable_timing=True)
-        g0.record(stream)
-        reps = 5
-        for _ in range(reps):
-            dist.all_gather_into_tensor(gathered, D)
-        g1.record(stream)
-        torch.cuda.synchronize()
-        ag_ms = g0.elapsed_time(g1) / reps
-        t = torch.tensor([ag_ms], device=dev, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ag_ms = float(t.item())
-        nbytes = D.numel() * D.element_size()
-        allgather = {"ms": ag_ms, "bytes_per_rank": nbytes,
-                     "bus_gbs": nbytes * (world - 1) / (ag_ms * 1e-3) / 1e9}
-
-        # ---- fused gather: the GEMM's epilogue stores this rank's shard into every rank's
-        # gathered D over NVLink (CUDA IPC peer pointers); no collective on the data path ----
-        fused = {"unavailable": "fused gather skipped"}
-        ok_local, handle = 1, (None, 0)
-        gathered2 = torch.empty((M, N * world), dtype=tdt, device=dev)
-        try:
-            handle = lib.ipc_export(gathered2)
-        except Exception as e:  # reported, and every rank skips together
-            ok_local, fused = 0, {"unavailable": f"ipc export: {e}"}
-        handles = [None] * world
-        dist.all_gather_object(handles, handle)
-        dsts, bases = [], []
-        for r in range(world):
-            if r == rank:
-                dsts.append(gathered2.data_ptr())
-            elif ok_local and handles[r][0] is not None:
-                try:
-                    base, ptr = lib.ipc_import(*handles[r])
-                    bases.append(base)
-                    dsts.append(ptr)
-                except Exception as e:
-                    ok_local, fused = 0, {"unavailable": f"ipc import: {e}"}
-            else:
-                ok_local = 0
-        flag = torch.tensor([ok_local], device=dev, dtype=torch.int32)
-        dist.all_reduce(flag, op=dist.ReduceOp.MIN)
-        if int(flag.item()) == 1:
-            def fstep():
-                lib.gemm_gather(ot, M, N, Kp, A, Bt, sA, sB, dsts, N * world, rank * N, rb, rb,
-                                ws if wsb else None, wsb, stream=stream)
-
-            for _ in range(2):
-                fstep()
-            torch.cuda.synchronize()
-            fail = torch.tensor([0 if lib.last_error() == lib.OK else 1], device=dev, dtype=torch.int32)
-            dist.all_reduce(fail, op=dist.ReduceOp.MAX)
-            if int(fail.item()) == 0:
-                reps = 5
-                fts = []
-                for i in range(reps):
-                    dist.barrier()
-                    flush.fill_(i & 0xFF)
-                    torch.cuda.synchronize()
-                    f0 = torch.cuda.Event(enable_timing=True)
-                    f1 = torch.cuda.Event(enable_timing=True)
-                    f0.record(stream)
-                    fstep()
-                    f1.record(stream)
-                    torch.cuda.synchronize()
-                    fts.append(f0.elapsed_time(f1))
-                f_ms = sum(fts) / len(fts)
-                t = torch.tensor([f_ms], device=dev, dtype=torch.float64)
-                dist.all_reduce(t, op=dist.ReduceOp.MAX)
-                f_ms = float(t.item())
-                dist.barrier()  # every rank's peer stores have landed
-                same = all(torch.equal(gathered2[:, r * N:(r + 1) * N].view(torch.int16 if tdt != torch.float32
-                                                                            else torch.int32),
-                                       gathered[r].view(torch.int16 if tdt != torch.float32 else torch.int32))
-                           for r in range(world))
-                sflag = torch.tensor([1 if same else 0], device=dev, dtype=torch.int32)
-                dist.all_reduce(sflag, op=dist.ReduceOp.MIN)
-                fused = {"ms": f_ms, "gemm_then_nccl_allgather_ms": ms + ag_ms,
-                         "speedup_vs_gemm_then_allgather": (ms + ag_ms) / f_ms,
-                         "nvlink_bytes_per_rank": nbytes * (world - 1),
-                         "matches_nccl_allgather": bool(sflag.item() == 1),
-                         "device_status": lib.device_status(),
-                         "what": "mxfp6_gemm_gather: epilogue stores each D chunk into all ranks' gathered "
-                                 "[M][N*world] outputs through CUDA IPC peer pointers"}
-            else:
-                fused = {"unavailable": "mxfp6_gemm_gather rejected the call on some rank"}
-        torch.cuda.synchronize()
-        dist.barrier()
-        for base in bases:
-            lib.ipc_close(base)
-        dist.barrier()
-        allgather["fused_gather"] = fused
-        del gathered, gathered2
 
     # ---- the reference's own timing convention (tests/test_gemm.cpp:32-52 of eeezio/mxfp6-gemm):
     # 8 warm-ups, then 20 back-to-back calls between two events, best of 4 repetitions; no L2
@@ -726,20 +982,31 @@ def run_ours(args):
                   "how": "8 warm-ups, 20 back-to-back calls between events, best of 4 (no L2 flush)"}
 
     vs_cublas = run_vs_cublas(M, N, K, step, stream, flush, dev) if args.vs_cublas and world == 1 else None
+    route = lib.route(ot, M, N, Kp)  # tile and K splits
+    out_bytes = D.element_size()
+    del A, sA, Bt, sB, D, ws
+
+    # ---- BASELINE config 5 split column-parallel over the ranks (every N), other configs (N=1) ----
+    strong = None
+    if not args.no_strong:
+        strong = strong_leg(lib, torch, dist, dev, stream, flush, rank, world, max(5, min(args.steps, 20)),
+                            max(3, args.warmup), not args.no_allgather, not args.no_per_config)
+    per_config = None
+    if world == 1 and not args.no_per_config:
+        per_config = per_config_leg(lib, torch, dev, stream, flush, max(5, min(args.steps, 20)),
+                                    max(3, args.warmup), args.config)
+        if strong is not None and args.config != "cfg5":
+            per_config["cfg5"] = {k: v for k, v in strong.items()
+                                  if k not in ("one_gpu", "efficiency_vs_one_gpu", "N_total", "N_per_gpu")}
+            per_config["cfg5"]["N"] = CONFIGS["cfg5"][1]
 
     # ---- CPU baseline (rank 0, N=1 only) ----
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
-        v, kind_s, cores, sample, _ = cpu_reference_sample(args.config, target_s=args.ref_seconds)
+        v, kind_s, cores, sample, _ = cpu_reference_sample(args.config, N, target_s=args.ref_seconds)
         cpu = {"value": v, "unit": "TFLOPS", "cores": cores, "kind": kind_s, "sample": sample}
 
-    bf16_peak, hbm_peak, basis = load_peaks()
-    out_bytes = {lib.OutType.F32: 4, lib.OutType.F16: 2, lib.OutType.BF16: 2}[ot]
-    algo_bytes = (M + N) * Kp * 3 // 4 + (M + N) * (Kp // 32) + M * N * out_bytes
-    peak = 2.0 * bf16_peak
-    kernel_ms = min(per)  # dominant kernel: the GEMM (plus the split-K reduce when routed)
-    achieved = flops_rank / (ms * 1e-3) / 1e12
-    route = lib.route(ot, M, N, Kp)  # tile and K splits
+    rf = roofline_fields(M, N, K, Kp, out_bytes, ms, wsb)
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": "TFLOPS", "n_gpus": world, "steps": args.steps,
@@ -747,23 +1014,16 @@ def run_ours(args):
             "scaling": "strong" if args.strong else "weak",
             "vs_baseline": None, "dtype": "fp6_e2m3 x fp6_e2m3 -> f32 accumulate",
             "data": "synthetic (seeded E2M3 codes uniform over 64 codes, E8M0 exponents per BASELINE)",
-            "config": {"workload": CONFIG_DESC[args.config] + (f", N-sharded over {world} GPUs (per-GPU shard N={N})"
-                                                               if world > 1 else "")
-                       + (f", the shard of one GPU out of {shards} (N={N} of {n_total})"
-                          if world == 1 and shards > 1 else ""),
-                       "M": M, "N_per_gpu": N, "N_total": n_total, "K": K, "out": out_name,
-                       "route": route,
-                       "parallelism": f"N-sharded x{world}, no collective on the GEMM path",
-                       "l2": "256 MiB buffer written before every timed step (L2 flushed)"},
-            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                         "frac": achieved / peak, "traffic": NCU_TRAFFIC_BYTES.get(args.config) if world == 1 else None,
-                         "algorithmic_bytes": algo_bytes,
-                         "peak_basis": f"2 x {basis} cuBLAS bf16 dense ({bf16_peak:.1f} TFLOP/s): B200's dense "
-                                       f"FP8/FP6 tensor rate is twice bf16",
-                         "best_step_ms": kernel_ms,
-                         "frac_of_nominal_fp6_dense": achieved / NOMINAL_FP6_TFLOPS,
-                         "algorithmic_gbs": algo_bytes / (ms * 1e-3) / 1e9,
-                         "splitk_workspace_bytes": 2 * wsb},  # partials written, then read by the reduce
+            "config": config,
+            "route": route,
+            "roofline": {"bound": "tensor", "achieved": rf["tflops"], "peak": rf["peak"], "unit": "TFLOP/s",
+                         "frac": rf["frac"], "traffic": NCU_TRAFFIC_BYTES.get(args.config) if world == 1 else None,
+                         "algorithmic_bytes": rf["algorithmic_bytes"],
+                         "peak_basis": rf["peak_basis"] + ": B200's dense FP8/FP6 tensor rate is twice bf16",
+                         "best_step_ms": min(per),
+                         "frac_of_nominal_fp6_dense": rf["frac_of_nominal_fp6_dense"],
+                         "algorithmic_gbs": rf["algorithmic_gbs"],
+                         "splitk_workspace_bytes": rf["splitk_workspace_bytes"]},  # partials written, then read
             "cpu_baseline": cpu,
             "e2e": {"value": e2e_value, "unit": "TFLOPS", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "ms_per_step": e2e_ms, "bitwise_equal_to_device_run": e2e_same,
@@ -775,12 +1035,10 @@ def run_ours(args):
             "clocks": clk.summary(),
             "device_status": status,
         }
-        if allgather:
-            line["allgather"] = allgather
-        if quant:
-            line["quantize_device"] = quant
-        if imp_leg:
-            line["import_ref_B_device"] = imp_leg
+        if strong:
+            line["strong"] = strong
+        if per_config:
+            line["per_config"] = per_config
         if compact:
             line["compact_a"] = compact
         if as_ref:
@@ -801,7 +1059,9 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", choices=sorted(CONFIGS), default="cfg2")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
-    ap.add_argument("--no-allgather", action="store_true")
+    ap.add_argument("--no-allgather", action="store_true", help="skip the gathers of the config-5 D shards")
+    ap.add_argument("--no-strong", action="store_true", help="skip the config-5 column-split leg")
+    ap.add_argument("--no-per-config", action="store_true", help="skip the other BASELINE configs (N=1)")
     ap.add_argument("--with-compact", action="store_true",
                     help="also time the same GEMM with A in the reference's compact layout (loader warps)")
     ap.add_argument("--ref-seconds", type=float, default=10.0, help="target CPU seconds per reference sample")
@@ -820,6 +1080,7 @@ def main():
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3
     if args.import_only:
+        sys.path.insert(0, PKG_DIR)
         import torch
 
         import mxfp6_b200 as lib

@@ -1,6 +1,10 @@
-"""Host logic of bench.py that needs no GPU: the end-to-end pipeline's upload order."""
+"""Host logic of bench.py that needs no GPU: the end-to-end pipeline's upload order, the operand
+generator and config shared by both arms, and the reference arm's isolation from the product library."""
 from __future__ import annotations
 
+import os
+
+import numpy as np
 import pytest
 
 
@@ -21,3 +25,48 @@ def test_upload_order_for_cfg2_keeps_bytes_balanced():
     import bench
     order = bench.e2e_upload_order(8, 4, 1024 * 6144, 2048 * 6144)
     assert [t for t, _ in order] == list("BAABAABAABAA")
+
+
+def test_bench_generator_matches_package_synth():
+    """bench.py's numpy generator (used by both arms) draws exactly the operands of the package's
+    synth.make_operands(kind="codes"), which the parity tests use."""
+    import bench
+    from mxfp6_b200.synth import make_operands
+    for M, N, K, er in [(256, 384, 512, (120, 134)), (128, 256, 1000, (118, 136))]:
+        A, sA, Bt, sB = bench.synth_codes(M, N, K, 11, er)
+        ops = make_operands(M, N, K, kind="codes", seed=11, exp_range=er)
+        for a, b in ((A, ops.A), (sA, ops.sA), (Bt, ops.Bt), (sB, ops.sB)):
+            assert a.dtype == b.dtype and np.array_equal(a, b)
+
+
+def test_bench_config_is_shared_by_both_arms():
+    import bench
+    c = bench.bench_config("cfg2", 4, 1)
+    assert c["N_per_gpu"] == 8192 and c["N_total"] == 4 * 8192
+    s = bench.bench_config("cfg5", 1, 8)
+    assert s["N_per_gpu"] == 3584 and s["N_total"] == 28672
+    assert "route" not in c  # the route needs the product library; it is a separate key
+
+
+def test_reference_arm_maps_no_product_library(tmp_path):
+    """The reference arm times the reference's CPU GEMM on operands from bench.py's own numpy
+    generator: neither the package nor libmxfp6gemm.so is loaded into its process."""
+    import json
+    import subprocess
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    code = (
+        "import sys, json, bench\n"
+        "class A: pass\n"
+        "a = A(); a.config = 'cfg1'; a.strong = False; a.shard_of = 1; a.steps = 1; a.warmup = 1\n"
+        "a.ref_seconds = 0.2\n"
+        "bench.run_reference_arm(a)\n"
+        "maps = open('/proc/self/maps').read()\n"
+        "print(json.dumps({'pkg': 'mxfp6_b200' in sys.modules, 'so': 'libmxfp6gemm' in maps}))\n")
+    r = subprocess.run([sys.executable, "-c", code], cwd=root, capture_output=True, text=True, timeout=600,
+                       env={**os.environ, "PYTHONPATH": root})
+    assert r.returncode == 0, r.stderr[-2000:]
+    lines = [json.loads(x) for x in r.stdout.strip().splitlines()]
+    ref_line, probe = lines[0], lines[-1]
+    assert probe == {"pkg": False, "so": False}
+    assert ref_line["impl"] == "reference" and ref_line["config"] == __import__("bench").bench_config("cfg1", 1, 1)
