@@ -111,6 +111,12 @@ void mxfp6_choose_tile(int M, int N, int Kp, int* out4);
  * and the number of K splits into out[0..2]. FP32 output may split where FP16/BF16 does not. */
 void mxfp6_route(int ot, int M, int N, int Kp, int* out3);
 
+/* How the CTA-pair route cuts the tiles of a partial last wave along N (no counterpart in the
+ * reference): 1 = not cut, 2 or 4 = each such tile runs as 2 or 4 sub-tiles of 128 or 64
+ * columns side by side. The cut changes only the schedule: every output element sums the same
+ * products in the same K order, so results are identical with and without it. */
+int mxfp6_route_tail_parts(int ot, int M, int N, int Kp);
+
 /* K granule (128) and K padded to it. */
 int mxfp6_k_tile(void);
 int mxfp6_kpad(int K);
@@ -124,6 +130,13 @@ void mxfp6_gemm_force_tile(int ot, int M, int N, int Kp, int MT, int NT, int spl
                            int A_row_bytes, int B_row_bytes, void* ws, size_t ws_bytes,
                            void* stream);
 
+/* Test hook (no counterpart in the reference): mxfp6_gemm_force_tile plus the CTA pair's cut of
+ * a partial last wave (tail_parts 1, or 2 / 4 with MT = NT = 256; see mxfp6_route_tail_parts).
+ * mxfp6_gemm_force_tile runs with tail_parts = 1. */
+void mxfp6_gemm_force_route(int ot, int M, int N, int Kp, int MT, int NT, int splits, int tail_parts,
+                            const void* dA, const void* dBsh, const uint8_t* dsA, const uint8_t* dsB, void* dD,
+                            int A_row_bytes, int B_row_bytes, void* ws, size_t ws_bytes, void* stream);
+
 /* No counterpart in the reference. The same computation as mxfp6_gemm_stream, for callers that
  * cannot call cudaMalloc: for example a plugin inside a host application that owns every device
  * allocation through its own pool, or a foreign-function binding that only forwards pointers it
@@ -132,7 +145,8 @@ void mxfp6_gemm_force_tile(int ot, int M, int N, int Kp, int MT, int NT, int spl
  * 32 MiB), which every GPU that loads the library reserves until the process exits. A shape whose
  * split needs more than that is rejected with MXFP6_ERR_WORKSPACE and nothing is launched.
  * The first call on a device looks up the array's device address (cudaGetSymbolAddress) with
- * that device current; make that first call before any stream capture. All calls share the one
+ * that device current; make that first call before any stream capture. A lookup that fails is
+ * not remembered: the next call on that device tries again. All calls share the one
  * array and it keeps the last call's contents (every partial is written before it is read, so
  * nothing needs clearing); calls that overlap on the GPU, on any streams, race on it. */
 void mxfp6_gemm_static_workspace(int ot, int M, int N, int Kp, const void* dA, const void* dBsh,
@@ -150,15 +164,17 @@ const char* mxfp6_last_error_string(void);
  * clears them. Returns -1 if the synchronisation itself failed. */
 int mxfp6_device_status(void);
 
+/* No counterpart in the reference (whose kernels have no bounded waits). Sets the cycle budget
+ * of the bounded barrier waits inside the GEMM kernels that this host thread launches from now
+ * on; cycles <= 0 restores the default (4e9 cycles, about 2 s). Returns the previous setting
+ * (0 = default). It exists to exercise the timeout path: with a budget far below the work, the
+ * kernels give up, set MXFP6_DEV_* bits, wait out their copies and MMAs in flight, free tensor
+ * memory and return; their outputs are then incomplete, and mxfp6_device_status() reports the
+ * bits. Production callers leave it at the default. */
+long long mxfp6_set_wait_budget(long long cycles);
+
 /* Number of kernels this library has launched in this process (all devices). */
 uint64_t mxfp6_launch_count(void);
-
-/* Diagnostic (no counterpart in the reference): one tensor-memory-accelerator load of a
- * 128-element x `rows` box of packed FP6 (16U6 unpack mode, optional 128-byte swizzle) into
- * shared memory, reported to an mbarrier that expects `expect_bytes`; the shared-memory box
- * (rows*128 bytes) and a completion flag (int) are written to dout. Returns an mxfp6_status. */
-int mxfp6_probe_tma_fp6(const void* dsrc, int rows, int Kp, int row_bytes, int swizzle128,
-                        uint32_t expect_bytes, void* dout);
 
 /* ---- host preprocessing (C face of include/mxfp6/preprocess.hpp) --------------------------
  * All buffers are host memory, caller-allocated. Sizes: packed row = 3*cols/4 bytes,

@@ -30,7 +30,12 @@ void note_launch();
 namespace {
 
 thread_local int t_last_error = MXFP6_OK;
+thread_local long long t_wait_budget = 0;  // 0: the kernels' default (kern::WAIT_BUDGET)
 std::atomic<uint64_t> g_launches{0};
+
+long long wait_budget() {
+    return t_wait_budget > 0 ? t_wait_budget : kern::WAIT_BUDGET;
+}
 
 void set_error(int code, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
 void set_error(int code, const char* fmt, ...) {
@@ -369,7 +374,10 @@ bool launch_gemm(int M, int N, int Kp, const void* dA, const void* dB, const uin
     p.splits = splits;
     p.out_align32 = (PARTIAL ? aligned(ws, 32) : dst_align32(dl, sizeof(OutT))) ? 1 : 0;
     set_compact(p, Kp, dA, A_row_bytes);
+    p.wait_budget = wait_budget();
     const long long tiles = (long long)p.m_blocks * p.n_blocks * splits;
+    p.tail_first = (int)tiles;
+    p.tail_parts = 1;
     const int grid = (int)(tiles < sm_count() ? tiles : sm_count());
     kernel<<<grid, kern::threads_for(AMODE), C::SMEM_BYTES, stream>>>(tmA, tmB, p);
     cudaError_t e = cudaGetLastError();
@@ -383,7 +391,7 @@ bool launch_gemm(int M, int N, int Kp, const void* dA, const void* dB, const uin
 
 template <typename OutT, bool PARTIAL, int AMODE>
 bool launch_pair(int M, int N, int Kp, const void* dA, const void* dB, const uint8_t* sA, const uint8_t* sB,
-                 const kern::DstList& dl, float* ws, int A_row_bytes, int B_row_bytes, int splits,
+                 const kern::DstList& dl, float* ws, int A_row_bytes, int B_row_bytes, int splits, int tail_parts,
                  cudaStream_t stream) {
     using C = kern::PairConfig<AMODE>;
     auto kernel = kern::gemm_mxfp6_sm100_pair<OutT, PARTIAL, AMODE>;
@@ -401,13 +409,25 @@ bool launch_pair(int M, int N, int Kp, const void* dA, const void* dB, const uin
         set_error(MXFP6_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(attr_err));
         return false;
     }
-    CUtensorMap tmA, tmB, tmSA, tmSB;
+    // The persistent pairs take units round-robin: whole tiles, then, when the last wave would be
+    // partial, its tiles cut along N into tail_parts sub-tiles (their B rows through tmBt, whose
+    // box is the sub-tile's half width).
+    const int m_blocks = (M + C::BM - 1) / C::BM, n_blocks = (N + C::BN - 1) / C::BN;
+    const long long tiles = (long long)m_blocks * n_blocks * splits;
+    const int pairs = sm_count() / 2;
+    if (tail_parts != 1 && tail_parts != 2 && tail_parts != 4) tail_parts = 1;
+    const long long rem = tiles % pairs;
+    if (rem == 0) tail_parts = 1;
+    const long long tail_first = tail_parts > 1 ? tiles - rem : tiles;
+    CUtensorMap tmA, tmB, tmSA, tmSB, tmBt;
     if (!make_a_tmap(AMODE, &tmA, dA, M, Kp, A_row_bytes, 128) || !make_fp6_tmap(&tmB, dB, N, Kp, B_row_bytes, 128) ||
-        !make_sf_tmap(&tmSA, sA, M, Kp, 1, C::SUB) || !make_sf_tmap_x4(&tmSB, sB, N, Kp)) {
+        !make_sf_tmap(&tmSA, sA, M, Kp, 1, C::SUB) || !make_sf_tmap_x4(&tmSB, sB, N, Kp) ||
+        (tail_parts > 1 && !make_fp6_tmap(&tmBt, dB, N, Kp, B_row_bytes, 128 / tail_parts))) {
         set_error(MXFP6_ERR_CUDA, "cuTensorMapEncodeTiled failed for %dx%dx%d (status %d)", M, N, Kp,
                   t_encode_status);
         return false;
     }
+    if (tail_parts == 1) tmBt = tmB;
     kern::Params p;
     p.sfA = sA;
     p.sfB = sB;
@@ -416,14 +436,16 @@ bool launch_pair(int M, int N, int Kp, const void* dA, const void* dB, const uin
     p.M = M;
     p.N = N;
     p.Kp = Kp;
-    p.m_blocks = (M + C::BM - 1) / C::BM;
-    p.n_blocks = (N + C::BN - 1) / C::BN;
+    p.m_blocks = m_blocks;
+    p.n_blocks = n_blocks;
     p.k_slabs = Kp / kern::BK;
     p.splits = splits;
     p.out_align32 = (PARTIAL ? aligned(ws, 32) : dst_align32(dl, sizeof(OutT))) ? 1 : 0;
     set_compact(p, Kp, dA, A_row_bytes);
-    const long long units = (long long)p.m_blocks * p.n_blocks * splits;
-    const int pairs = sm_count() / 2;
+    p.wait_budget = wait_budget();
+    p.tail_first = (int)tail_first;
+    p.tail_parts = tail_parts;
+    const long long units = tail_first + (tiles - tail_first) * tail_parts;
     const int clusters = (int)(units < pairs ? units : pairs);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * clusters, 1, 1);
@@ -437,7 +459,7 @@ bool launch_pair(int M, int N, int Kp, const void* dA, const void* dB, const uin
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, tmA, tmB, tmSA, tmSB, p);
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, tmA, tmB, tmSA, tmSB, tmBt, p);
     if (e == cudaSuccess) e = cudaGetLastError();
     if (e != cudaSuccess) {
         set_error(MXFP6_ERR_CUDA, "pair GEMM launch failed: %s", cudaGetErrorString(e));
@@ -473,8 +495,9 @@ bool run_route(const Route& r, int M, int N, int Kp, const void* dA, const void*
     const bool part = r.splits > 1;
     bool ok;
     if (r.MT == 256) {
-        ok = part ? launch_pair<float, true, AMODE>(M, N, Kp, dA, dB, sA, sB, dl, wsf, Ar, Br, r.splits, stream)
-                  : launch_pair<OutT, false, AMODE>(M, N, Kp, dA, dB, sA, sB, dl, wsf, Ar, Br, 1, stream);
+        ok = part ? launch_pair<float, true, AMODE>(M, N, Kp, dA, dB, sA, sB, dl, wsf, Ar, Br, r.splits, r.tail_parts,
+                                                    stream)
+                  : launch_pair<OutT, false, AMODE>(M, N, Kp, dA, dB, sA, sB, dl, wsf, Ar, Br, 1, r.tail_parts, stream);
     } else if (r.NT == 256) {
         ok = part ? launch_gemm<256, float, true, AMODE>(M, N, Kp, dA, dB, sA, sB, dl, wsf, Ar, Br, r.splits,
                                                            stream)
@@ -572,15 +595,23 @@ void gemm_entry(int ot, int M, int N, int Kp, const void* dA, const void* dB, co
 constexpr size_t kStaticWorkspaceBytes = size_t(32) << 20;
 static __device__ __align__(256) unsigned char g_static_split_ws[kStaticWorkspaceBytes];
 void* g_static_ws_addr[kMaxDevices];
-cudaError_t g_static_ws_err[kMaxDevices];
-std::once_flag g_static_ws_once[kMaxDevices];
+std::mutex g_static_ws_mutex[kMaxDevices];
 
-void* static_workspace_address(int dev) {
-    std::call_once(g_static_ws_once[dev], [dev] {
+// Only a successful lookup is cached: a lookup that failed (inside a stream capture, say) is
+// retried by the next call on that device. The runtime's sticky error from a failed lookup is
+// cleared so that it does not surface in the caller's next error check; the failure itself is
+// reported through *err.
+void* static_workspace_address(int dev, cudaError_t* err) {
+    std::lock_guard<std::mutex> lock(g_static_ws_mutex[dev]);
+    *err = cudaSuccess;
+    if (!g_static_ws_addr[dev]) {
         void* addr = nullptr;
-        g_static_ws_err[dev] = cudaGetSymbolAddress(&addr, g_static_split_ws);
-        g_static_ws_addr[dev] = g_static_ws_err[dev] == cudaSuccess ? addr : nullptr;
-    });
+        *err = cudaGetSymbolAddress(&addr, g_static_split_ws);
+        if (*err == cudaSuccess && addr)
+            g_static_ws_addr[dev] = addr;
+        else
+            cudaGetLastError();
+    }
     return g_static_ws_addr[dev];
 }
 
@@ -673,6 +704,10 @@ void mxfp6_route(int ot, int M, int N, int Kp, int* out3) {
     out3[2] = r.splits;
 }
 
+int mxfp6_route_tail_parts(int ot, int M, int N, int Kp) {
+    return route_for_out(ot, M, N, Kp).tail_parts;
+}
+
 int mxfp6_k_tile(void) {
     return K_TILE;
 }
@@ -681,11 +716,14 @@ int mxfp6_kpad(int K) {
     return kpad(K);
 }
 
-void mxfp6_gemm_force_tile(int ot, int M, int N, int Kp, int MT, int NT, int splits, const void* dA,
-                           const void* dBsh, const uint8_t* dsA, const uint8_t* dsB, void* dD,
-                           int A_row_bytes, int B_row_bytes, void* ws, size_t ws_bytes,
-                           void* stream) {
+void mxfp6_gemm_force_route(int ot, int M, int N, int Kp, int MT, int NT, int splits, int tail_parts, const void* dA,
+                            const void* dBsh, const uint8_t* dsA, const uint8_t* dsB, void* dD, int A_row_bytes,
+                            int B_row_bytes, void* ws, size_t ws_bytes, void* stream) {
     t_last_error = MXFP6_OK;
+    if (tail_parts != 1 && (MT != 256 || (tail_parts != 2 && tail_parts != 4))) {
+        set_error(MXFP6_ERR_UNSUPPORTED, "tail cut %d: 1, or 2 or 4 on the 256x256 pair tile", tail_parts);
+        return;
+    }
     if (!validate(ot, M, N, Kp, dA, dBsh, dsA, dsB, dD, A_row_bytes, B_row_bytes)) return;
     const bool tile_ok = (MT == 256 && NT == 256) || (MT == 128 && (NT == 128 || NT == 256));
     if (!tile_ok || splits < 1 || splits > Kp / K_TILE) {
@@ -698,8 +736,16 @@ void mxfp6_gemm_force_tile(int ot, int M, int N, int Kp, int MT, int NT, int spl
                   splitk_bytes(M, N, splits), ws_bytes);
         return;
     }
-    run(ot, Route{MT, NT, splits}, M, N, Kp, dA, dBsh, dsA, dsB, single_dst(dD, N), A_row_bytes, B_row_bytes, ws,
-        static_cast<cudaStream_t>(stream));
+    run(ot, Route{MT, NT, splits, tail_parts}, M, N, Kp, dA, dBsh, dsA, dsB, single_dst(dD, N), A_row_bytes,
+        B_row_bytes, ws, static_cast<cudaStream_t>(stream));
+}
+
+void mxfp6_gemm_force_tile(int ot, int M, int N, int Kp, int MT, int NT, int splits, const void* dA,
+                           const void* dBsh, const uint8_t* dsA, const uint8_t* dsB, void* dD,
+                           int A_row_bytes, int B_row_bytes, void* ws, size_t ws_bytes,
+                           void* stream) {
+    mxfp6_gemm_force_route(ot, M, N, Kp, MT, NT, splits, 1, dA, dBsh, dsA, dsB, dD, A_row_bytes, B_row_bytes, ws,
+                           ws_bytes, stream);
 }
 
 void mxfp6_gemm_static_workspace(int ot, int M, int N, int Kp, const void* dA, const void* dBsh,
@@ -723,10 +769,11 @@ void mxfp6_gemm_static_workspace(int ot, int M, int N, int Kp, const void* dA, c
             set_error(MXFP6_ERR_CUDA, "no CUDA device");
             return;
         }
-        ws = static_workspace_address(dev);
+        cudaError_t lookup_err = cudaSuccess;
+        ws = static_workspace_address(dev, &lookup_err);
         if (!ws) {
             set_error(MXFP6_ERR_CUDA, "cudaGetSymbolAddress for the static split-K workspace failed: %s",
-                      cudaGetErrorString(g_static_ws_err[dev]));
+                      cudaGetErrorString(lookup_err));
             return;
         }
     }
@@ -802,6 +849,12 @@ int mxfp6_ipc_import(const void* handle, size_t offset, void** base_out, void** 
 
 int mxfp6_ipc_close(void* base) {
     return cudaIpcCloseMemHandle(base) == cudaSuccess ? MXFP6_OK : MXFP6_ERR_CUDA;
+}
+
+long long mxfp6_set_wait_budget(long long cycles) {
+    const long long prev = t_wait_budget;
+    t_wait_budget = cycles > 0 ? cycles : 0;
+    return prev;
 }
 
 size_t mxfp6_static_workspace_bytes(void) {

@@ -51,7 +51,9 @@ constexpr int GROUP_M = 16;
 constexpr int NUM_THREADS = 192;    // 6 warps
 constexpr int EPI_WARP0 = 2;        // first epilogue warp
 constexpr int A_TMA_BYTES = BM * BK * 3 / 4;  // packed bytes one A slab moves
-constexpr long long WAIT_BUDGET = 4000000000LL;  // cycles (about 2 s at 1.9 GHz)
+// Default cycle budget of a bounded wait (about 2 s at 1.9 GHz); Params::wait_budget carries
+// the one a launch uses. Drains after a timeout always use WAIT_BUDGET / 4.
+constexpr long long WAIT_BUDGET = 4000000000LL;
 
 template <int BN, int AMODE = A_TMA>
 struct Config {
@@ -95,6 +97,11 @@ struct Params {
     // compact A (software producer, compact_a.cuh): packed rows, stride and valid bytes per row
     const uint8_t* a_ptr;
     int a_stride, a_valid;
+    long long wait_budget;  // cycles a role waits on a barrier before it gives up (WAIT_BUDGET by default)
+    // Pair kernel only: the tiles from tail_first on (the last, partial wave of the persistent
+    // schedule) are each cut along N into tail_parts sub-tiles of 256 / tail_parts columns, so
+    // that more CTA pairs share the last wave. 1 = no cut (tail_first is then the tile count).
+    int tail_first, tail_parts;
 };
 
 struct TileCoord {
@@ -276,13 +283,16 @@ __global__ void __launch_bounds__(threads_for(AMODE), 1)
     const uint32_t tmem_base = *tmem_slot;
 
     const int total_tiles = p.m_blocks * p.n_blocks * p.splits;
+    // Abort bookkeeping, read after the roles have finished (see the end of the kernel): the
+    // producer's last load per stage and its phase parity, and whether any MMA was issued.
+    uint32_t issued_mask = 0, issued_phase = 0;
+    bool mma_issued = false;
 
     if (warp == 0) {
         if (lane == 0) {
             // ---------------- TMA producer ----------------
             int stage = 0;
             uint32_t phase = 0;
-            uint32_t issued_mask = 0, issued_phase = 0;  // per stage: outstanding load + parity
             bool ok = true;
             for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
                 const TileCoord tc = decode_tile(t, p);
@@ -292,7 +302,7 @@ __global__ void __launch_bounds__(threads_for(AMODE), 1)
                     if (tc.nb * BN + j * 128 < p.N) sfb_atoms++;
                 const uint32_t tx = (COMPACT ? 0u : (uint32_t)A_TMA_BYTES) + C::B_TMA_BYTES + 512u * (1 + sfb_atoms);
                 for (int i = 0; i < tc.kb_count; i++) {
-                    if (!sm100::wait_parity_bounded(empty_bar(stage), phase ^ 1u, abort_flag, WAIT_BUDGET)) {
+                    if (!sm100::wait_parity_bounded(empty_bar(stage), phase ^ 1u, abort_flag, p.wait_budget)) {
                         if (!*abort_flag) raise_status(0x1u, abort_flag);
                         ok = false;
                         break;
@@ -317,19 +327,6 @@ __global__ void __launch_bounds__(threads_for(AMODE), 1)
                     }
                 }
             }
-            if (!ok && COMPACT) {
-                // The full barriers also count loader arrivals that may never come: give the
-                // tensor loads in flight time to land instead.
-                sm100::settle_ns(200000);
-            } else if (!ok) {
-                // Let every load still in flight land before shared memory is released.
-                const int zero = 0;
-                for (int s = 0; s < C::STAGES; s++)
-                    if ((issued_mask >> s) & 1u)
-                        if (!sm100::wait_parity_bounded(full_bar(s), (issued_phase >> s) & 1u, &zero,
-                                                        WAIT_BUDGET / 4))
-                            atomicOr(&g_device_status, 0x8u);
-            }
         }
     } else if (warp == 1) {
         if (lane == 0) {
@@ -337,17 +334,17 @@ __global__ void __launch_bounds__(threads_for(AMODE), 1)
             constexpr uint32_t idesc = sm100::make_idesc_e2m3(BM, BN);
             int stage = 0;
             uint32_t phase = 0, acc_phase = 0;
-            bool ok = true, issued = false;
+            bool ok = true;
             for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
                 const TileCoord tc = decode_tile(t, p);
-                if (!sm100::wait_parity_bounded(acc_empty, acc_phase ^ 1u, abort_flag, WAIT_BUDGET)) {
+                if (!sm100::wait_parity_bounded(acc_empty, acc_phase ^ 1u, abort_flag, p.wait_budget)) {
                     if (!*abort_flag) raise_status(0x2u, abort_flag);
                     ok = false;
                     break;
                 }
                 sm100::tc_fence_after();
                 for (int i = 0; i < tc.kb_count; i++) {
-                    if (!sm100::wait_parity_bounded(full_bar(stage), phase, abort_flag, WAIT_BUDGET)) {
+                    if (!sm100::wait_parity_bounded(full_bar(stage), phase, abort_flag, p.wait_budget)) {
                         if (!*abort_flag) raise_status(0x2u, abort_flag);
                         ok = false;
                         break;
@@ -371,7 +368,7 @@ __global__ void __launch_bounds__(threads_for(AMODE), 1)
                                                (tmem_base + C::TMEM_SFA) | sel,
                                                (tmem_base + C::TMEM_SFB) | sel, (i > 0 || k > 0) ? 1u : 0u);
                     }
-                    issued = true;
+                    mma_issued = true;
                     sm100::tc_commit(empty_bar(stage));
                     if (++stage == C::STAGES) {
                         stage = 0;
@@ -381,13 +378,6 @@ __global__ void __launch_bounds__(threads_for(AMODE), 1)
                 if (!ok) break;
                 sm100::tc_commit(acc_full);
                 acc_phase ^= 1u;
-            }
-            if (!ok && issued) {
-                // Wait for every MMA and copy already issued before tensor memory is freed.
-                const int zero = 0;
-                sm100::tc_commit(drain_bar);
-                if (!sm100::wait_parity_bounded(drain_bar, 0, &zero, WAIT_BUDGET / 4))
-                    atomicOr(&g_device_status, 0x8u);
             }
         }
     } else if (AMODE == A_CPASYNC && warp >= LOADER_WARP0) {
@@ -402,7 +392,7 @@ __global__ void __launch_bounds__(threads_for(AMODE), 1)
             for (int i = 0; i < tc.kb_count; i++) {
                 int got = 1;
                 if (lane == 0)
-                    got = sm100::wait_parity_bounded(empty_bar(stage), phase ^ 1u, abort_flag, WAIT_BUDGET) ? 1 : 0;
+                    got = sm100::wait_parity_bounded(empty_bar(stage), phase ^ 1u, abort_flag, p.wait_budget) ? 1 : 0;
                 got = __shfl_sync(0xffffffffu, got, 0);
                 if (!got) {
                     if (lane == 0 && !*abort_flag) raise_status(0x1u, abort_flag);
@@ -426,7 +416,7 @@ __global__ void __launch_bounds__(threads_for(AMODE), 1)
         uint32_t acc_phase = 0;
         for (int t = blockIdx.x; t < total_tiles; t += gridDim.x) {
             const TileCoord tc = decode_tile(t, p);
-            if (!sm100::wait_parity_bounded(acc_full, acc_phase, abort_flag, WAIT_BUDGET)) {
+            if (!sm100::wait_parity_bounded(acc_full, acc_phase, abort_flag, p.wait_budget)) {
                 if (!*abort_flag) raise_status(0x4u, abort_flag);
                 break;
             }
@@ -457,7 +447,34 @@ __global__ void __launch_bounds__(threads_for(AMODE), 1)
     }
 
     sm100::tc_fence_before();
-    __syncthreads();
+    // After a timeout anywhere in the CTA (any role may have given up while another finished
+    // normally), wait out everything still in flight before shared and tensor memory are
+    // released: the producer's loads that no MMA consumed, and every MMA and scale copy issued.
+    // Without an abort the epilogue has waited for every tile, so nothing is in flight. The barrier
+    // ORs every thread's view of the flag, so the whole CTA takes the same branch.
+    const int aborted = __syncthreads_or(*abort_flag != 0);
+    if (aborted) {
+        const int zero = 0;
+        if (warp == 0 && lane == 0) {
+            if (COMPACT) {
+                // The full barriers also count loader arrivals that may never come: give the
+                // tensor loads in flight time to land instead.
+                sm100::settle_ns(200000);
+            } else {
+                for (int s = 0; s < C::STAGES; s++)
+                    if ((issued_mask >> s) & 1u)
+                        if (!sm100::wait_parity_bounded(full_bar(s), (issued_phase >> s) & 1u, &zero,
+                                                        WAIT_BUDGET / 4))
+                            atomicOr(&g_device_status, 0x8u);
+            }
+        }
+        if (warp == 1 && lane == 0 && mma_issued) {
+            sm100::tc_commit(drain_bar);
+            if (!sm100::wait_parity_bounded(drain_bar, 0, &zero, WAIT_BUDGET / 4)) atomicOr(&g_device_status, 0x8u);
+        }
+        sm100::tc_fence_before();
+        __syncthreads();
+    }
     if (warp == 1) {
         __syncwarp();
         sm100::tc_fence_after();

@@ -20,6 +20,11 @@
 //     down and buffer 1 from its bottom chunk up, so the overlap chunk is read first and the
 //     next tile's MMAs may start as soon as that one chunk has left tensor memory; the rest of
 //     the epilogue runs under the next tile's main loop.
+//   * The persistent pairs take 256 x 256 tiles round-robin. When the last wave would be partial,
+//     its tiles are cut along N into 2 or 4 sub-tiles (128 or 64 columns, all K slabs each) so
+//     that more pairs share it: a sub-tile's MMAs have N = 128 or 64, its B rows come through a
+//     second tensor map with the narrower box, and the MMA reads B's scales from the sub-tile's
+//     own first tensor-memory column. Each output element still sums its K slabs in order.
 //   * No TMA multicast anywhere: each CTA fetches its own operands.
 //   * A compact A (a row stride the 16U6 load cannot address) is copied into the A stages by
 //     four extra loader warps per CTA instead (AMODE = A_CPASYNC, compact_a.cuh).
@@ -48,10 +53,6 @@ struct PairConfig {
     // 128x256b tensor-memory copy, which fills all four lane quarters without broadcasting.
     static constexpr int SFB_BYTES = 4 * 1024;
     static constexpr int SF_STAGE = SFA_BYTES + SFB_BYTES;
-    static constexpr uint32_t SLAB_TX = 2 * (128 * BK * 3 / 4);  // packed A + B bytes per CTA
-    static constexpr uint32_t tx_stage(int nsub) {                // leader's barrier counts both CTAs
-        return 2 * (nsub * SLAB_TX + SF_STAGE);
-    }
     static constexpr int TMEM_COLS = 512;
     static constexpr int BUF1_COL = 224;  // buffer 1 starts 32 columns below buffer 0's end
     static constexpr int TMEM_SFB = 480;  // B scales: 8 columns (8-column aligned for the wide copy)
@@ -67,6 +68,36 @@ __device__ __forceinline__ void store_cluster_u32(uint32_t cluster_addr, uint32_
     asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(cluster_addr), "r"(v) : "memory");
 }
 
+// One work unit of the pair kernel: a 256 x 256 tile (a split-K segment of one, with splits), or,
+// from p.tail_first on, one of the p.tail_parts sub-tiles that a tile of the last, partial wave
+// is cut into along N (256 / tail_parts columns, all of its K slabs). Cutting along N keeps every
+// output element's K summation whole and in order, so results do not depend on the cut.
+struct PairUnit {
+    TileCoord tc;
+    int n0;     // first output column
+    int width;  // output columns: 256, or 256 / tail_parts
+};
+
+__device__ __forceinline__ int pair_units(const Params& p) {
+    const int tiles = p.m_blocks * p.n_blocks * p.splits;
+    return p.tail_first + (tiles - p.tail_first) * p.tail_parts;
+}
+
+__device__ __forceinline__ PairUnit decode_unit(int t, const Params& p) {
+    PairUnit u;
+    if (t < p.tail_first) {
+        u.tc = decode_tile(t, p);
+        u.width = 256;
+        u.n0 = u.tc.nb * 256;
+    } else {
+        const int v = t - p.tail_first;
+        u.tc = decode_tile(p.tail_first + v / p.tail_parts, p);
+        u.width = 256 / p.tail_parts;
+        u.n0 = u.tc.nb * 256 + (v % p.tail_parts) * u.width;
+    }
+    return u;
+}
+
 // AMODE (compact_a.cuh): A_TMA loads A with the 16U6 tensor load; A_CPASYNC adds four
 // loader warps per CTA that build the A image from p.a_ptr, and whose arrivals join the leader's
 // full barrier.
@@ -74,10 +105,10 @@ template <typename OutT, bool PARTIAL, int AMODE = A_TMA>
 __global__ void __launch_bounds__(threads_for(AMODE), 1)
     gemm_mxfp6_sm100_pair(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                           const __grid_constant__ CUtensorMap tmSA, const __grid_constant__ CUtensorMap tmSB,
-                          const Params p) {
+                          const __grid_constant__ CUtensorMap tmBt, const Params p) {
     using C = PairConfig<AMODE>;
     constexpr bool COMPACT = AMODE != A_TMA;
-    static_assert(!COMPACT || C::SUB == 1, "the compact-A loaders fill one 128-deep slab per stage");
+    static_assert(C::SUB == 1, "one 128-deep slab per stage");
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     const uint32_t raw_u32 = sm100::smem_u32(smem_raw);
     const uint32_t base = (raw_u32 + 1023u) & ~1023u;
@@ -132,6 +163,7 @@ __global__ void __launch_bounds__(threads_for(AMODE), 1)
         sm100::prefetch_tmap(&tmB);
         sm100::prefetch_tmap(&tmSA);
         sm100::prefetch_tmap(&tmSB);
+        if (p.tail_parts > 1) sm100::prefetch_tmap(&tmBt);
     }
 
     if (warp == 1) {
@@ -144,41 +176,47 @@ __global__ void __launch_bounds__(threads_for(AMODE), 1)
     sm100::tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
 
-    const int total_tiles = p.m_blocks * p.n_blocks * p.splits;
+    const int total_units = pair_units(p);
     const int cluster_id = blockIdx.x >> 1;
     const int num_clusters = gridDim.x >> 1;
+    // Abort bookkeeping, read after the roles have finished (see the end of the kernel): the
+    // producer's last load per stage and its phase parity, and whether any MMA was issued.
+    uint32_t issued_mask = 0, issued_phase = 0;
+    bool mma_issued = false;
 
     if (warp == 0) {
         if (lane == 0) {
             // ---------------- TMA producer (both CTAs) ----------------
             int stage = 0;
             uint32_t phase = 0;
-            uint32_t issued_mask = 0, issued_phase = 0;
             bool ok = true;
-            for (int t = cluster_id; t < total_tiles && ok; t += num_clusters) {
-                const TileCoord tc = decode_tile(t, p);
+            for (int t = cluster_id; t < total_units && ok; t += num_clusters) {
+                const PairUnit u = decode_unit(t, p);
+                if (u.n0 >= p.N) continue;  // a tail sub-tile wholly past N: no work
+                const TileCoord& tc = u.tc;
                 const int a_row = tc.mb * C::BM + 128 * (int)rank;
-                const int b_row = tc.nb * C::BN + 128 * (int)rank;
-                for (int i = 0; i < tc.kb_count; i += C::SUB) {
-                    if (!sm100::wait_parity_bounded(empty_bar(stage), phase ^ 1u, abort_flag, WAIT_BUDGET)) {
+                // each CTA holds half of the unit's B^T rows (128 for a full tile)
+                const int half = u.width / 2;
+                const int b_row = u.n0 + half * (int)rank;
+                const CUtensorMap* tmb = u.width == C::BN ? &tmB : &tmBt;
+                // the leader's barrier counts both CTAs' bytes: A (unless compact), B, scales
+                const uint32_t tx = 2u * ((COMPACT ? 0u : (uint32_t)A_TMA_BYTES) + (uint32_t)half * (BK * 3 / 4) +
+                                          (uint32_t)C::SF_STAGE);
+                for (int i = 0; i < tc.kb_count; i++) {
+                    if (!sm100::wait_parity_bounded(empty_bar(stage), phase ^ 1u, abort_flag, p.wait_budget)) {
                         if (!*abort_flag) raise(0x1u);
+                        *abort_flag = 1;
                         ok = false;
                         break;
                     }
                     const int kb = tc.kb_begin + i;
-                    const int nsub = tc.kb_count - i < C::SUB ? tc.kb_count - i : C::SUB;
                     const uint32_t fb = sm100::mapa_shared(full_bar(stage), 0);
-                    if (rank == 0)
-                        sm100::mbar_arrive_expect_tx(full_bar(stage),
-                                                     C::tx_stage(nsub) - (COMPACT ? nsub * C::SLAB_TX : 0u));
+                    if (rank == 0) sm100::mbar_arrive_expect_tx(full_bar(stage), tx);
                     const uint32_t a_dst = ab_base + stage * C::AB_STAGE;
-                    for (int j = 0; j < nsub; j++) {
-                        if (!COMPACT)
-                            sm100::tma_load_2d_pair(a_dst + j * C::SLAB_BYTES, &tmA, fb, (kb + j) * BK, a_row);
-                        sm100::tma_load_2d_pair(a_dst + C::A_BYTES + j * C::SLAB_BYTES, &tmB, fb, (kb + j) * BK,
-                                                b_row);
-                    }
-                    // scale atoms past the last row block read as zero
+                    if (!COMPACT) sm100::tma_load_2d_pair(a_dst, &tmA, fb, kb * BK, a_row);
+                    sm100::tma_load_2d_pair(a_dst + C::A_BYTES, tmb, fb, kb * BK, b_row);
+                    // scale atoms past the last row block read as zero; a sub-tile's scales lie in
+                    // its tile's two B atoms
                     const uint32_t sf_dst = sf_base + stage * C::SF_STAGE;
                     sm100::tma_load_3d_pair(sf_dst, &tmSA, fb, 0, kb, tc.mb * 2 + (int)rank);
                     sm100::tma_load_4d_pair(sf_dst + C::SFA_BYTES, &tmSB, fb, 0, 0, kb, tc.nb * 2);
@@ -190,43 +228,37 @@ __global__ void __launch_bounds__(threads_for(AMODE), 1)
                     }
                 }
             }
-            if (!ok) {
-                const int zero = 0;
-                if (rank == 0 && !COMPACT) {
-                    for (int s = 0; s < C::STAGES; s++)
-                        if ((issued_mask >> s) & 1u)
-                            if (!sm100::wait_parity_bounded(full_bar(s), (issued_phase >> s) & 1u, &zero,
-                                                                    WAIT_BUDGET / 4))
-                                atomicOr(&g_device_status, 0x8u);
-                } else {
-                    // the peer's loads report to the leader (and in compact mode the full barriers
-                    // also count loader arrivals that may never come): give them time to land
-                    sm100::settle_ns(200000);
-                }
-            }
         }
     } else if (warp == 1) {
         if (lane == 0 && rank == 0) {
             // ---------------- MMA issuer (leader only) ----------------
-            constexpr uint32_t idesc = sm100::make_idesc_e2m3(C::BM, C::BN);
-            uint32_t idesc_k[BK / 32];
-#pragma unroll
-            for (int k = 0; k < BK / 32; k++) idesc_k[k] = sm100::idesc_with_sf_ids(idesc, k, k);
             const uint64_t a_desc0 = sm100::make_kmajor_sw128_desc(ab_base);
             const uint64_t b_desc0 = sm100::make_kmajor_sw128_desc(ab_base + C::A_BYTES);
             int stage = 0;
             uint32_t phase = 0;
-            bool ok = true, issued = false;
-            int local = 0;
-            for (int t = cluster_id; t < total_tiles && ok; t += num_clusters, local++) {
-                const TileCoord tc = decode_tile(t, p);
+            bool ok = true;
+            int local = 0;  // units this pair has computed: selects the accumulator buffer
+            for (int t = cluster_id; t < total_units && ok; t += num_clusters) {
+                const PairUnit u = decode_unit(t, p);
+                if (u.n0 >= p.N) continue;
+                const TileCoord& tc = u.tc;
+                // N = the unit's width; scale id k selects byte k of each scale word
+                uint32_t idesc_k[BK / 32];
+                const uint32_t idesc = sm100::make_idesc_e2m3(C::BM, u.width);
+#pragma unroll
+                for (int k = 0; k < BK / 32; k++) idesc_k[k] = sm100::idesc_with_sf_ids(idesc, k, k);
+                // B's scales sit in 8 tensor-memory columns, one per 32 columns of the tile; a
+                // sub-tile starts at its own first column
+                const uint32_t sfb_t = tmem_base + C::TMEM_SFB + (uint32_t)(u.n0 - tc.nb * C::BN) / 32u;
+                const uint32_t sfa_t = tmem_base + C::TMEM_SFA;
                 const int b = local & 1;
                 const uint32_t d_taddr = tmem_base + (b ? C::BUF1_COL : 0);
                 if (!sm100::wait_parity_bounded(acc_empty0 + 8u * b, ((local >> 1) & 1) ^ 1u, abort_flag,
-                                                        WAIT_BUDGET) ||
+                                                        p.wait_budget) ||
                     (local >= 1 && !sm100::wait_parity_bounded(ovl_free, (local - 1) & 1, abort_flag,
-                                                                       WAIT_BUDGET))) {
+                                                                       p.wait_budget))) {
                     if (!*abort_flag) raise(0x2u);
+                    *abort_flag = 1;
                     ok = false;
                     break;
                 }
@@ -235,30 +267,25 @@ __global__ void __launch_bounds__(threads_for(AMODE), 1)
                 // slab's barrier without blocking right after issuing the current one, and
                 // blocks only when that slab's data has not landed yet.
                 bool ready = sm100::mbar_test_wait(full_bar(stage), phase);
-                for (int i = 0; i < tc.kb_count; i += C::SUB) {
-                    if (!ready && !sm100::wait_parity_bounded(full_bar(stage), phase, abort_flag, WAIT_BUDGET)) {
+                for (int i = 0; i < tc.kb_count; i++) {
+                    if (!ready && !sm100::wait_parity_bounded(full_bar(stage), phase, abort_flag, p.wait_budget)) {
                         if (!*abort_flag) raise(0x2u);
+                        *abort_flag = 1;
                         ok = false;
                         break;
                     }
-                    const int nsub = tc.kb_count - i < C::SUB ? tc.kb_count - i : C::SUB;
                     const uint32_t sf_src = sf_base + stage * C::SF_STAGE;
                     // A's atom: one broadcast copy; B's two atoms, staged four times over: one wide copy
                     sm100::tc_cp_32x128b_warpx4_pair(tmem_base + C::TMEM_SFA, sm100::make_sf_desc(sf_src));
                     sm100::tc_cp_128x256b_pair(tmem_base + C::TMEM_SFB, sm100::make_sf_wide_desc(sf_src + C::SFA_BYTES));
-                    for (int j = 0; j < nsub; j++) {
-                        const uint32_t sfa_t = tmem_base + C::TMEM_SFA;
-                        const uint32_t sfb_t = tmem_base + C::TMEM_SFB;
-                        const uint32_t off16 = (uint32_t)(stage * C::AB_STAGE + j * C::SLAB_BYTES) >> 4;
+                    const uint32_t off16 = (uint32_t)(stage * C::AB_STAGE) >> 4;
 #pragma unroll
-                        for (int k = 0; k < BK / 32; k++) {
-                            const uint32_t sel = (uint32_t)k << 30;
-                            sm100::tc_mma_mxf8f6f4_pair(d_taddr, a_desc0 + off16 + 2 * k, b_desc0 + off16 + 2 * k,
-                                                        idesc_k[k], sfa_t | sel, sfb_t | sel,
-                                                        (i > 0 || j > 0 || k > 0) ? 1u : 0u);
-                        }
+                    for (int k = 0; k < BK / 32; k++) {
+                        const uint32_t sel = (uint32_t)k << 30;
+                        sm100::tc_mma_mxf8f6f4_pair(d_taddr, a_desc0 + off16 + 2 * k, b_desc0 + off16 + 2 * k,
+                                                    idesc_k[k], sfa_t | sel, sfb_t | sel, (i > 0 || k > 0) ? 1u : 0u);
                     }
-                    issued = true;
+                    mma_issued = true;
                     sm100::tc_commit_pair(empty_bar(stage), 0x3);
                     if (++stage == C::STAGES) {
                         stage = 0;
@@ -268,12 +295,7 @@ __global__ void __launch_bounds__(threads_for(AMODE), 1)
                 }
                 if (!ok) break;
                 sm100::tc_commit_pair(acc_full0 + 8u * b, 0x3);
-            }
-            if (!ok && issued) {
-                const int zero = 0;
-                sm100::tc_commit_pair(drain_bar, 0x1);
-                if (!sm100::wait_parity_bounded(drain_bar, 0, &zero, WAIT_BUDGET / 4))
-                    atomicOr(&g_device_status, 0x8u);
+                local++;
             }
         } else if (AMODE == A_CPASYNC && lane == 0) {
             // ---------------- relay (peer only, A_CPASYNC) ----------------
@@ -282,11 +304,14 @@ __global__ void __launch_bounds__(threads_for(AMODE), 1)
             int stage = 0;
             uint32_t phase = 0;
             bool ok = true;
-            for (int t = cluster_id; t < total_tiles && ok; t += num_clusters) {
-                const TileCoord tc = decode_tile(t, p);
+            for (int t = cluster_id; t < total_units && ok; t += num_clusters) {
+                const PairUnit u = decode_unit(t, p);
+                if (u.n0 >= p.N) continue;
+                const TileCoord& tc = u.tc;
                 for (int i = 0; i < tc.kb_count; i++) {
-                    if (!sm100::wait_parity_bounded(full_bar(stage), phase, abort_flag, WAIT_BUDGET)) {
+                    if (!sm100::wait_parity_bounded(full_bar(stage), phase, abort_flag, p.wait_budget)) {
                         if (!*abort_flag) raise(0x1u);
+                        *abort_flag = 1;
                         ok = false;
                         break;
                     }
@@ -307,16 +332,19 @@ __global__ void __launch_bounds__(threads_for(AMODE), 1)
         int stage = 0;
         uint32_t phase = 0;
         bool ok = true;
-        for (int t = cluster_id; t < total_tiles && ok; t += num_clusters) {
-            const TileCoord tc = decode_tile(t, p);
+        for (int t = cluster_id; t < total_units && ok; t += num_clusters) {
+            const PairUnit u = decode_unit(t, p);
+            if (u.n0 >= p.N) continue;
+            const TileCoord& tc = u.tc;
             const int a_row = tc.mb * C::BM + 128 * (int)rank;
             for (int i = 0; i < tc.kb_count; i++) {
                 int got = 1;
                 if (lane == 0)
-                    got = sm100::wait_parity_bounded(empty_bar(stage), phase ^ 1u, abort_flag, WAIT_BUDGET) ? 1 : 0;
+                    got = sm100::wait_parity_bounded(empty_bar(stage), phase ^ 1u, abort_flag, p.wait_budget) ? 1 : 0;
                 got = __shfl_sync(0xffffffffu, got, 0);
                 if (!got) {
                     if (lane == 0 && !*abort_flag) raise(0x1u);
+                    *abort_flag = 1;
                     ok = false;
                     break;
                 }
@@ -336,39 +364,48 @@ __global__ void __launch_bounds__(threads_for(AMODE), 1)
         const uint32_t t_lane = tmem_base + ((uint32_t)(32 * quarter) << 16);
         const uint32_t leader_acc_empty = sm100::mapa_shared(acc_empty0, 0);
         const uint32_t leader_ovl_free = sm100::mapa_shared(ovl_free, 0);
-        int local = 0;
-        for (int t = cluster_id; t < total_tiles; t += num_clusters, local++) {
-            const TileCoord tc = decode_tile(t, p);
+        int local = 0;  // units this pair has computed: selects the accumulator buffer
+        for (int t = cluster_id; t < total_units; t += num_clusters) {
+            const PairUnit u = decode_unit(t, p);
+            if (u.n0 >= p.N) continue;
+            const TileCoord& tc = u.tc;
+            const int nchunks = u.width / 32;  // 32-column chunks of this unit's accumulator
             const int b = local & 1;
             // One lane per warp polls the barrier (fewer pollers on shared memory while the main
             // loop runs); the warp then confirms the completed phase without blocking.
             int got = 1;
             if (lane == 0)
-                got = sm100::wait_parity_bounded(acc_full0 + 8u * b, (local >> 1) & 1, abort_flag, WAIT_BUDGET) ? 1 : 0;
+                got = sm100::wait_parity_bounded(acc_full0 + 8u * b, (local >> 1) & 1, abort_flag, p.wait_budget) ? 1 : 0;
             got = __shfl_sync(0xffffffffu, got, 0);
             if (!got) {
                 if (lane == 0 && !*abort_flag) raise(0x4u);
+                *abort_flag = 1;
                 break;
             }
             sm100::mbar_try_wait(acc_full0 + 8u * b, (local >> 1) & 1);
             sm100::tc_fence_after();
             const int row = tc.mb * C::BM + 128 * (int)rank + 32 * quarter + lane;
-            const int col0 = tc.nb * C::BN;
+            const int col0 = u.n0;
             const bool regroup = !PARTIAL && p.dst.n > 1;
             uint32_t pend[16];  // FP16/BF16 with several destinations: first chunk of a 64-column pair
 #pragma unroll 1
             for (int j = 0; j < C::BN / 32; j++) {
-                // buffer 0 top-down, buffer 1 bottom-up: the shared chunk [224, 256) goes first
+                // buffer 0 top-down, buffer 1 bottom-up: the shared chunk [224, 256) goes first.
+                // A sub-tile fills only its first nchunks chunks (an even number, so the chunk
+                // pairs below stay aligned); the shared chunk is still released at j == 0.
                 const int c = b ? j : (C::BN / 32 - 1 - j);
                 const uint32_t tcol = (b ? C::BUF1_COL : 0) + 32 * c;
                 uint32_t r[32];
-                sm100::tmem_ld_32x32b_x32(t_lane + tcol, r);
-                sm100::tmem_ld_wait();
+                if (c < nchunks) {
+                    sm100::tmem_ld_32x32b_x32(t_lane + tcol, r);
+                    sm100::tmem_ld_wait();
+                }
                 if (j == 0) {
                     sm100::tc_fence_before();
                     __syncwarp();
                     if (lane == 0) sm100::mbar_arrive_cluster(leader_ovl_free);
                 }
+                if (c >= nchunks) continue;
                 const int col = col0 + 32 * c;
                 if (regroup) {
                     // chunks are processed in pairs (c, c ^ 1) in both orders; col < N is uniform
@@ -409,11 +446,40 @@ __global__ void __launch_bounds__(threads_for(AMODE), 1)
             sm100::tc_fence_before();
             __syncwarp();
             if (lane == 0) sm100::mbar_arrive_cluster(leader_acc_empty + 8u * b);
+            local++;
         }
     }
 
     sm100::tc_fence_before();
-    __syncthreads();
+    // After a timeout anywhere in the pair, wait out everything still in flight before shared and
+    // tensor memory are released (any role may have given up while another finished normally):
+    // the leader's MMAs and scale copies, and the loads no MMA consumed. The leader's full
+    // barriers count both CTAs' bytes; the peer, whose loads report there, gives its own loads
+    // a bounded settle time. A role that leaves its loop on a timeout, its own or one it saw in
+    // the flag, sets this CTA's flag before the barrier above; without a timeout the epilogue has
+    // waited for every tile, so nothing is in flight. The peer may still set this CTA's flag
+    // remotely: the barrier ORs every thread's view of it, so the whole CTA takes the same branch.
+    const int aborted = __syncthreads_or(*abort_flag != 0);
+    if (aborted) {
+        const int zero = 0;
+        if (warp == 0 && lane == 0) {
+            if (rank == 0 && !COMPACT) {
+                for (int s = 0; s < C::STAGES; s++)
+                    if ((issued_mask >> s) & 1u)
+                        if (!sm100::wait_parity_bounded(full_bar(s), (issued_phase >> s) & 1u, &zero,
+                                                        WAIT_BUDGET / 4))
+                            atomicOr(&g_device_status, 0x8u);
+            } else {
+                sm100::settle_ns(200000);
+            }
+        }
+        if (warp == 1 && lane == 0 && rank == 0 && mma_issued) {
+            sm100::tc_commit_pair(drain_bar, 0x1);
+            if (!sm100::wait_parity_bounded(drain_bar, 0, &zero, WAIT_BUDGET / 4)) atomicOr(&g_device_status, 0x8u);
+        }
+        sm100::tc_fence_before();
+        __syncthreads();
+    }
     sm100::cluster_sync();  // no CTA leaves while its peer may still touch its shared memory
     if (warp == 1) {
         __syncwarp();

@@ -16,6 +16,10 @@
 //           + T_fixed                                      the kernel's start-up beyond the smallest
 //           + T_reduce + (2S + 1) * M*N*4 / HBM  when S > 1   reduce launch, partial write + read, D
 //
+// On the CTA pair a partial last wave is cut along N (pair_tail_parts): each of its tiles becomes
+// 2 or 4 sub-tiles that run side by side, so the last wave costs a fraction of a full one
+// (TAIL_FRACTION, measured) instead of a whole tile's time.
+//
 // T_slab is the time one SM (or pair) spends per slab: 256x256 and 128x256 tiles do the same
 // MMA work per SM per slab; their constants reflect how well each keeps the tensor pipe fed
 // (measured: the pair sustains more, the narrow tile pays for streaming A at half the work).
@@ -29,10 +33,29 @@ struct Route {
     int MT;      // tile rows: 256 = CTA pair, 128 = single CTA
     int NT;      // tile columns
     int splits;  // K segments (1 = no split)
+    int tail_parts = 1;  // CTA pair: N-cuts of each tile of a partial last wave (1, 2 or 4)
 };
 
 inline size_t splitk_bytes(int M, int N, int splits) {
     return (size_t)splits * (size_t)M * (size_t)N * sizeof(float);
+}
+
+// N-cuts of each tile of the CTA pair's last wave when that wave is partial: the finest cut
+// (64-column sub-tiles) whose sub-tiles all fit in one wave of `slots` pairs, else 128-column
+// sub-tiles, else none. `units` counts 256 x 256 tiles times split segments.
+inline int pair_tail_parts(long long units, long long slots) {
+    if (units <= 0 || slots <= 0) return 1;
+    const long long rem = units % slots;
+    if (rem == 0) return 1;
+    if (rem * 4 <= slots) return 4;
+    if (rem * 2 <= slots) return 2;
+    return 1;
+}
+
+// Time of a last wave cut into `parts` sub-tiles, as a fraction of a full wave: the sub-tiles
+// still stream all of A's rows, so they are bound by A's loads rather than by the MMAs.
+inline double pair_tail_fraction(int parts) {
+    return parts >= 4 ? 0.45 : (parts == 2 ? 0.6 : 1.0);
 }
 
 inline double route_cost_us(int M, int N, int Kp, int MT, int NT, int S, int sms) {
@@ -63,10 +86,14 @@ inline double route_cost_us(int M, int N, int Kp, int MT, int NT, int S, int sms
     }
     const long long units = (long long)((M + MT - 1) / MT) * ((N + NT - 1) / NT) * S;
     const long long slots = sms / per_unit > 0 ? sms / per_unit : 1;
-    const long long waves = (units + slots - 1) / slots;
     const int slabs = Kp / 128;
     const int per = (slabs + S - 1) / S;
-    double t = (double)waves * (per * t_slab + t_tile) + t_fixed;
+    double waves = (double)((units + slots - 1) / slots);
+    if (MT == 256 && units >= slots) {  // the cut's saving is measured behind full waves only
+        const int parts = pair_tail_parts(units, slots);
+        if (parts > 1) waves = (double)(units / slots) + pair_tail_fraction(parts);
+    }
+    double t = waves * (per * t_slab + t_tile) + t_fixed;
     if (S > 1) t += T_REDUCE_LAUNCH + (2.0 * S + 1.0) * (double)M * N * 4.0 / HBM;
     return t;
 }
@@ -106,6 +133,10 @@ inline Route route_for(int M, int N, int Kp, int sms, int min_splits = 1) {
                 first = false;
             }
         }
+    }
+    if (best.MT == 256) {
+        const long long units = (long long)((M + 255) / 256) * ((N + 255) / 256) * best.splits;
+        best.tail_parts = pair_tail_parts(units, sms / 2 > 0 ? sms / 2 : 1);
     }
     return best;
 }

@@ -48,6 +48,11 @@ _force = _fn("mxfp6_gemm_force_tile", None,
              [C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p,
               C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_size_t,
               C.c_void_p])
+_force_route = _fn("mxfp6_gemm_force_route", None,
+                   [C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_void_p,
+                    C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_size_t,
+                    C.c_void_p])
+_route_tail = _fn("mxfp6_route_tail_parts", C.c_int, [C.c_int, C.c_int, C.c_int, C.c_int])
 _static_ws_gemm = _fn("mxfp6_gemm_static_workspace", None,
                       [C.c_int, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
                        C.c_void_p, C.c_int, C.c_int, C.c_void_p])
@@ -72,6 +77,7 @@ last_error = _fn("mxfp6_last_error", C.c_int, [])
 _last_error_string = _fn("mxfp6_last_error_string", C.c_char_p, [])
 _device_status = _fn("mxfp6_device_status", C.c_int, [])
 launch_count = _fn("mxfp6_launch_count", C.c_uint64, [])
+set_wait_budget = _fn("mxfp6_set_wait_budget", C.c_longlong, [C.c_longlong])  # this thread's kernels; <= 0: default
 _quantize = _fn("mxfp6_quantize", None, [_f32p, C.c_int, C.c_int, _u8p, _u8p, C.c_int])
 _quantize_dev = _fn("mxfp6_quantize_device", C.c_int,
                     [C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_int, C.c_void_p])
@@ -90,8 +96,6 @@ _untile = _fn("mxfp6_untile_scales", None, [_u8p, C.c_int, C.c_int, _u8p])
 _imp_B = _fn("mxfp6_import_ref_B", C.c_int, [_u8p, C.c_int, C.c_int, _u8p, C.c_int])
 _imp_sc = _fn("mxfp6_import_ref_scales", C.c_int, [_u8p, C.c_int, C.c_int, C.c_int, C.c_int, _u8p])
 _repad = _fn("mxfp6_repad_rows", C.c_int, [_u8p, C.c_int, C.c_int, C.c_int, _u8p, C.c_int])
-_probe = _fn("mxfp6_probe_tma_fp6", C.c_int,
-             [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_uint32, C.c_void_p])
 
 # status codes (enum mxfp6_status)
 OK, ERR_INVALID_SHAPE, ERR_INVALID_STRIDE, ERR_MISALIGNED, ERR_NULL_POINTER = 0, 1, 2, 3, 4
@@ -138,10 +142,11 @@ def choose_tile(M: int, N: int, Kp: int) -> TileChoice:
 
 
 def route(ot, M: int, N: int, Kp: int) -> dict:
-    """The route gemm() takes for output type ot: tile and K splits (mxfp6_route)."""
+    """The route gemm() takes for output type ot: tile, K splits (mxfp6_route) and the CTA pair's
+    N-cut of a partial last wave (mxfp6_route_tail_parts)."""
     out = (C.c_int * 3)()
     _route(int(ot), M, N, Kp, out)
-    return {"MT": out[0], "NT": out[1], "splits": out[2]}
+    return {"MT": out[0], "NT": out[1], "splits": out[2], "tail_parts": _route_tail(int(ot), M, N, Kp)}
 
 
 def gemm_workspace_size(M: int, N: int, Kp: int, ot=None) -> int:
@@ -179,6 +184,14 @@ def gemm_force_tile(ot, M, N, Kp, MT, NT, splits, dA, dBsh, dsA, dsB, dD, A_row_
     s = 0 if stream is None else (stream.cuda_stream if hasattr(stream, "cuda_stream") else _addr(stream))
     _force(int(ot), M, N, Kp, MT, NT, splits, _addr(dA), _addr(dBsh), _addr(dsA), _addr(dsB), _addr(dD),
            A_row_bytes, B_row_bytes, _addr(ws), ws_bytes, s)
+
+
+def gemm_force_route(ot, M, N, Kp, MT, NT, splits, tail_parts, dA, dBsh, dsA, dsB, dD, A_row_bytes, B_row_bytes,
+                     ws=None, ws_bytes=0, stream=None):
+    """Test hook: gemm_force_tile plus the CTA pair's N-cut of a partial last wave (1, 2 or 4)."""
+    s = 0 if stream is None else (stream.cuda_stream if hasattr(stream, "cuda_stream") else _addr(stream))
+    _force_route(int(ot), M, N, Kp, MT, NT, splits, tail_parts, _addr(dA), _addr(dBsh), _addr(dsA), _addr(dsB),
+                 _addr(dD), A_row_bytes, B_row_bytes, _addr(ws), ws_bytes, s)
 
 
 def gemm_gather(ot, M, N, Kp, dA, dBsh, dsA, dsB, dDs, ldd, col0, A_row_bytes, B_row_bytes, ws=None, ws_bytes=0,
@@ -230,10 +243,6 @@ def last_error_string() -> str:
 def device_status() -> int:
     """Synchronise and return (then clear) the kernels' sticky status bits; -1 if sync failed."""
     return _device_status()
-
-
-def probe_tma_fp6(dsrc, rows, Kp, row_bytes, swizzle128, expect_bytes, dout) -> int:
-    return _probe(_addr(dsrc), rows, Kp, row_bytes, int(swizzle128), expect_bytes, _addr(dout))
 
 
 # ---- host layout producers (C++ header helpers through the C ABI) --------------------------------

@@ -29,14 +29,15 @@ class DeviceOperands:
 
 
 def run_gemm(dev: DeviceOperands, ot, ws_mode="sized", force=None, poison=True, stream=None):
-    """Run the routed GEMM (or a forced route (MT, NT, splits)); returns D as a torch CPU tensor."""
+    """Run the routed GEMM (or a forced route (MT, NT, splits[, tail_parts])); returns D as a torch
+    CPU tensor."""
     o = dev.ops
     D = torch.empty((o.M, o.N), dtype=TORCH_OUT[ot], device=dev.A.device)
     if poison:
         D.view(torch.uint8).fill_(0x5A)
     ws, wsb = None, 0
     if force is not None:
-        MT, NT, S = force
+        MT, NT, S = force[:3]
         if S > 1:
             wsb = S * o.M * o.N * 4
     elif ws_mode == "sized":
@@ -50,9 +51,12 @@ def run_gemm(dev: DeviceOperands, ot, ws_mode="sized", force=None, poison=True, 
     if force is None:
         lib.gemm(ot, o.M, o.N, o.Kp, dev.A, dev.Bt, dev.sA, dev.sB, D, o.row_bytes, o.row_bytes, ws, wsb,
                  stream=stream)
-    else:
+    elif len(force) == 3:
         lib.gemm_force_tile(ot, o.M, o.N, o.Kp, force[0], force[1], force[2], dev.A, dev.Bt, dev.sA, dev.sB, D,
                             o.row_bytes, o.row_bytes, ws, wsb, stream=stream)
+    else:  # (MT, NT, splits, tail_parts)
+        lib.gemm_force_route(ot, o.M, o.N, o.Kp, force[0], force[1], force[2], force[3], dev.A, dev.Bt, dev.sA,
+                             dev.sB, D, o.row_bytes, o.row_bytes, ws, wsb, stream=stream)
     err = lib.last_error()
     assert err == lib.OK, f"gemm rejected the call: {err} {lib.last_error_string()}"
     torch.cuda.synchronize()

@@ -1,18 +1,23 @@
-// Diagnostic entry point: one tensor-memory-accelerator load of a packed FP6 box through the
-// 16U6 unpack mode, dumped back to global memory. It pins, on the device, the two layout facts
-// the GEMM relies on: how 16 packed codes (12 bytes) land in a 16-byte shared-memory slot, and
-// how many bytes the load reports to its mbarrier (expect_bytes must match for the barrier to
-// complete; the wait is bounded, so a mismatch shows up as flag 0, not as a hang).
+// Test-only layout probe (built into tests/probe/libmxfp6probe.so, never into libmxfp6gemm.so):
+// one tensor-memory-accelerator load of a packed FP6 box through the 16U6 unpack mode, dumped
+// back to global memory. It pins, on the device, the two layout facts the GEMM kernels rely on:
+// how 16 packed codes (12 bytes) land in a 16-byte shared-memory slot, and that the load reports
+// 96 bytes per 128-code row to its mbarrier (the transaction count the kernels arm). The probe
+// arms exactly that count; no other count can be requested.
 #include <cuda.h>
 #include <cuda_runtime.h>
 
-#include <cstdio>
+#include <cstdint>
 
-#include "mxfp6_gemm.h"
 #include "sm100_ptx.cuh"
 
-namespace mxfp6 {
 namespace {
+
+using namespace mxfp6;
+
+constexpr int kOk = 0;
+constexpr int kBadArgs = 1;
+constexpr int kCuda = 6;
 
 __global__ void __launch_bounds__(32, 1)
     probe_tma_fp6_kernel(const __grid_constant__ CUtensorMap tm, uint32_t expect_bytes, int box_bytes,
@@ -42,18 +47,18 @@ __global__ void __launch_bounds__(32, 1)
 }
 
 }  // namespace
-}  // namespace mxfp6
 
-using namespace mxfp6;
-
-extern "C" int mxfp6_probe_tma_fp6(const void* dsrc, int rows, int Kp, int row_bytes, int swizzle128,
-                                   uint32_t expect_bytes, void* dout) {
-    if (!dsrc || !dout || rows <= 0 || rows > 256 || Kp % 128 || row_bytes % 32) return MXFP6_ERR_INVALID_SHAPE;
+// dsrc: packed FP6 rows [rows][row_bytes] on the device (row_bytes % 32 == 0, >= 96); Kp % 128 == 0;
+// rows in 1..256. dout receives rows*128 bytes of the shared-memory box and an int completion
+// flag. The mbarrier expects rows*96 bytes. Returns 0, or 1 for bad arguments, 6 for a CUDA error.
+extern "C" int mxfp6_probe_tma_fp6(const void* dsrc, int rows, int Kp, int row_bytes, int swizzle128, void* dout) {
+    if (!dsrc || !dout || rows <= 0 || rows > 256 || Kp < 128 || Kp % 128 || row_bytes % 32 || row_bytes < 96)
+        return kBadArgs;
     void* fnp = nullptr;
     cudaDriverEntryPointQueryResult q;
     if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fnp, cudaEnableDefault, &q) != cudaSuccess ||
         q != cudaDriverEntryPointSuccess || !fnp)
-        return MXFP6_ERR_CUDA;
+        return kCuda;
     using Fn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                             const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
                             CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
@@ -66,12 +71,12 @@ extern "C" int mxfp6_probe_tma_fp6(const void* dsrc, int rows, int Kp, int row_b
                                            dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                                            swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
                                            CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    if (r != CUDA_SUCCESS) return MXFP6_ERR_CUDA;
+    if (r != CUDA_SUCCESS) return kCuda;
     const int box_bytes = rows * 128;
     const int smem = 1024 + box_bytes + 64;
     if (cudaFuncSetAttribute(probe_tma_fp6_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
-        return MXFP6_ERR_CUDA;
-    probe_tma_fp6_kernel<<<1, 32, smem>>>(tm, expect_bytes, box_bytes, static_cast<uint8_t*>(dout));
-    if (cudaGetLastError() != cudaSuccess) return MXFP6_ERR_CUDA;
-    return MXFP6_OK;
+        return kCuda;
+    probe_tma_fp6_kernel<<<1, 32, smem>>>(tm, (uint32_t)rows * 96u, box_bytes, static_cast<uint8_t*>(dout));
+    if (cudaGetLastError() != cudaSuccess) return kCuda;
+    return kOk;
 }

@@ -3,8 +3,10 @@
 
 On one GPU: two local destinations of pitch 2N, at column 0 or N, on every route and output
 type; each must hold exactly the plain GEMM's D in its column range and keep its poison
-elsewhere. A D assembled block by block from one-destination calls matches the oracle. On two GPUs (skipped with fewer): each rank writes its shard into its own and its
-peer's gathered output through a CUDA IPC mapping; both ranks must end with [D_0 | D_1]."""
+elsewhere. A D assembled block by block from one-destination calls matches the oracle. Two
+ranks (processes), on two GPUs (skipped with fewer) and both on one GPU: each rank writes its
+shard into its own and its peer's gathered output through a CUDA IPC mapping; both ranks must
+end with [D_0 | D_1]."""
 from __future__ import annotations
 
 import os
@@ -114,8 +116,8 @@ def test_blocks_assembled_into_one_output(lib, oracle, ot):
     check(D.cpu(), ref, o, oracle, label=f"blocks {ra}x{rc} {ot}")
 
 
-def _rank_main(rank, world, port, out_q):
-    """One rank of the 2-GPU gather test (spawned process)."""
+def _rank_main(rank, world, port, out_q, device=None, shape=(512, 768, 1920)):
+    """One rank of the two-rank gather test (spawned process), on GPU `device` (default: its rank)."""
     try:
         sys.path.insert(0, os.path.join(os.path.dirname(HERE), "mxfp6-gemm_b200"))
         sys.path.insert(0, HERE)
@@ -124,10 +126,10 @@ def _rank_main(rank, world, port, out_q):
         import mxfp6_b200 as lib
         from mxfp6_b200.synth import make_operands
         from gpu_helpers import DeviceOperands, run_gemm
-        torch.cuda.set_device(rank)
+        torch.cuda.set_device(rank if device is None else device)
         dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
                                 timeout=timedelta(seconds=60))
-        M, N, K = 512, 768, 1920
+        M, N, K = shape
         a = make_operands(M, 128, K, kind="codes", seed=11)
         b = make_operands(128, N, K, kind="codes", seed=20 + rank)
         from mxfp6_b200.synth import Operands
@@ -171,9 +173,7 @@ def _rank_main(rank, world, port, out_q):
         out_q.put((rank, False, repr(e)))
 
 
-def test_two_gpu_gather_over_ipc():
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs 2 GPUs")
+def _run_two_ranks(device=None, shape=(512, 768, 1920)):
     import socket
     import torch.multiprocessing as mp
     s = socket.socket()
@@ -182,7 +182,7 @@ def test_two_gpu_gather_over_ipc():
     s.close()
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    procs = [ctx.Process(target=_rank_main, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_rank_main, args=(r, 2, port, q, device, shape)) for r in range(2)]
     for p in procs:
         p.start()
     results = []
@@ -193,3 +193,19 @@ def test_two_gpu_gather_over_ipc():
         if p.is_alive():
             p.kill()
     assert all(ok for _, ok, _ in results), results
+
+
+def test_two_gpu_gather_over_ipc():
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    _run_two_ranks()
+
+
+@pytest.mark.parametrize("shape", [(512, 768, 1920), (4096, 3584, 1024)])
+def test_two_process_gather_over_ipc_on_one_gpu(shape):
+    """The same two-rank exchange with both ranks' processes on GPU 0: each maps the other's
+    gathered output through CUDA IPC and the GEMM's epilogue stores into it, so the IPC-mapped
+    destination path runs even where only one GPU is available. No kernel waits on the other
+    rank (the host barrier orders them), so sharing the GPU is safe. Shapes on the 128 x 128
+    route and on the CTA pair with a cut last wave."""
+    _run_two_ranks(device=0, shape=shape)

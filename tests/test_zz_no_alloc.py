@@ -31,13 +31,16 @@ def test_static_workspace_rejects_oversized_split(lib, capfd):
     need = None
     for m, n, k in [(1024, 4096, 105728), (1536, 4096, 105728), (1024, 8192, 105728), (2048, 4096, 105728),
                     (1024, 6144, 105728), (512, 8192, 105728), (1024, 3840, 105728)]:
-        ws = lib.gemm_workspace_size(m, n, k)
+        # the query for the output type of the call below, so the call is refused on the host
+        ws = lib.gemm_workspace_size(m, n, k, lib.OutType.F32)
         if ws > lib.static_workspace_bytes():
             need = (m, n, k)
             break
     assert need is not None, "no test shape splits beyond the static workspace"
     m, n, k = need
+    assert lib.gemm_workspace_size(m, n, k, lib.OutType.F32) > lib.static_workspace_bytes()
     rb = k * 3 // 4
+    # The addresses are never dereferenced: the size check refuses the call before any launch.
     lib.gemm_static_workspace(lib.OutType.F32, m, n, k, 0x10000, 0x20000, 0x30000, 0x40000, 0x50000, rb, rb)
     assert lib.last_error() == lib.ERR_WORKSPACE
     assert "static workspace" in capfd.readouterr().err
