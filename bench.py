@@ -835,98 +835,106 @@ def run_ours(args):
     value = flops_rank * world / (ms * 1e-3) / 1e12
 
     # ---- end to end through the C ABI with host buffers ----
-    pinned = {k: v.cpu().pin_memory() for k, v in (("A", A), ("Bt", Bt), ("sA", sA), ("sB", sB))}
-    dA2, dB2, dsA2, dsB2 = (torch.empty_like(t) for t in (A, Bt, sA, sB))
-    Dh = torch.empty((M, N), dtype=tdt).pin_memory()
-    h2d = sum(p.numel() * p.element_size() for p in pinned.values())
-    d2h = Dh.numel() * Dh.element_size()
+    def e2e_leg():
+        pinned = {k: v.cpu().pin_memory() for k, v in (("A", A), ("Bt", Bt), ("sA", sA), ("sB", sB))}
+        dA2, dB2, dsA2, dsB2 = (torch.empty_like(t) for t in (A, Bt, sA, sB))
+        Dh = torch.empty((M, N), dtype=tdt).pin_memory()
+        h2d = sum(p.numel() * p.element_size() for p in pinned.values())
+        d2h = Dh.numel() * Dh.element_size()
 
-    # The step's transfers and math overlap in a two-dimensional block pipeline. A is cut into
-    # row chunks and B^T into row chunks (column chunks of B and D). The chunks go up on a copy
-    # stream in an order that keeps D blocks coming as early as possible (e2e_upload_order); a
-    # first block of D is computable after two chunks. Each block D[i, j] is one call of the
-    # library's public entry on the compute stream as soon as A_i and B_j have landed:
-    # mxfp6_gemm_gather with one destination (D's row i*mc) writes the block straight into D
-    # (row stride N, first column j*nc). Each block goes back on a third stream, as a pitched
-    # copy, as soon as it is computed. Every byte still crosses PCIe inside every step.
-    s_up = torch.cuda.Stream(dev)
-    s_down = torch.cuda.Stream(dev)
-    ra = E2E_ROW_CHUNKS if M % (128 * E2E_ROW_CHUNKS) == 0 else 1
-    rc = args.e2e_cols if args.e2e_cols > 0 and N % (128 * args.e2e_cols) == 0 else 1
-    mc, nc = M // ra, N // rc
-    sa_chunk = (mc // 128) * (Kp // 128) * 512  # scale atoms are row-block major
-    sb_chunk = (nc // 128) * (Kp // 128) * 512
-    ws_c, wsb_c = workspace(lib, torch, mc, nc, Kp, ot, dev)  # a block's own route may split K
-    order = e2e_upload_order(ra, rc, mc * rb, nc * rb)
-    memcpy2d = cudart_memcpy2d_async()
-    esz = Dh.element_size()
+        # The step's transfers and math overlap in a two-dimensional block pipeline. A is cut into
+        # row chunks and B^T into row chunks (column chunks of B and D). The chunks go up on a copy
+        # stream in an order that keeps D blocks coming as early as possible (e2e_upload_order); a
+        # first block of D is computable after two chunks. Each block D[i, j] is one call of the
+        # library's public entry on the compute stream as soon as A_i and B_j have landed:
+        # mxfp6_gemm_gather with one destination (D's row i*mc) writes the block straight into D
+        # (row stride N, first column j*nc). Each block goes back on a third stream, as a pitched
+        # copy, as soon as it is computed. Every byte still crosses PCIe inside every step.
+        s_up = torch.cuda.Stream(dev)
+        s_down = torch.cuda.Stream(dev)
+        ra = E2E_ROW_CHUNKS if M % (128 * E2E_ROW_CHUNKS) == 0 else 1
+        rc = args.e2e_cols if args.e2e_cols > 0 and N % (128 * args.e2e_cols) == 0 else 1
+        mc, nc = M // ra, N // rc
+        sa_chunk = (mc // 128) * (Kp // 128) * 512  # scale atoms are row-block major
+        sb_chunk = (nc // 128) * (Kp // 128) * 512
+        ws_c, wsb_c = workspace(lib, torch, mc, nc, Kp, ot, dev)  # a block's own route may split K
+        order = e2e_upload_order(ra, rc, mc * rb, nc * rb)
+        memcpy2d = cudart_memcpy2d_async()
+        esz = Dh.element_size()
 
-    def e2e_step():
-        ev_start = torch.cuda.Event()
-        ev_start.record(stream)
-        s_up.wait_event(ev_start)
-        have_a, have_b, blocks = [], [], []
-        with torch.cuda.stream(s_up):
-            for kind_c, k in order:
-                if kind_c == "A":
-                    dA2[k * mc:(k + 1) * mc].copy_(pinned["A"][k * mc:(k + 1) * mc], non_blocking=True)
-                    dsA2[k * sa_chunk:(k + 1) * sa_chunk].copy_(pinned["sA"][k * sa_chunk:(k + 1) * sa_chunk],
-                                                                non_blocking=True)
-                else:
-                    dB2[k * nc:(k + 1) * nc].copy_(pinned["Bt"][k * nc:(k + 1) * nc], non_blocking=True)
-                    dsB2[k * sb_chunk:(k + 1) * sb_chunk].copy_(pinned["sB"][k * sb_chunk:(k + 1) * sb_chunk],
-                                                                non_blocking=True)
+        def e2e_step():
+            ev_start = torch.cuda.Event()
+            ev_start.record(stream)
+            s_up.wait_event(ev_start)
+            have_a, have_b, blocks = [], [], []
+            with torch.cuda.stream(s_up):
+                for kind_c, k in order:
+                    if kind_c == "A":
+                        dA2[k * mc:(k + 1) * mc].copy_(pinned["A"][k * mc:(k + 1) * mc], non_blocking=True)
+                        dsA2[k * sa_chunk:(k + 1) * sa_chunk].copy_(pinned["sA"][k * sa_chunk:(k + 1) * sa_chunk],
+                                                                    non_blocking=True)
+                    else:
+                        dB2[k * nc:(k + 1) * nc].copy_(pinned["Bt"][k * nc:(k + 1) * nc], non_blocking=True)
+                        dsB2[k * sb_chunk:(k + 1) * sb_chunk].copy_(pinned["sB"][k * sb_chunk:(k + 1) * sb_chunk],
+                                                                    non_blocking=True)
+                    ev = torch.cuda.Event()
+                    ev.record(s_up)
+                    if kind_c == "A":
+                        blocks += [(k, j, ev) for j in have_b]
+                        have_a.append(k)
+                    else:
+                        blocks += [(i, k, ev) for i in have_a]
+                        have_b.append(k)
+            done = []
+            for i, j, ev in blocks:
+                stream.wait_event(ev)
+                lib.gemm_gather(ot, mc, nc, Kp, dA2[i * mc:], dB2[j * nc:], dsA2[i * sa_chunk:], dsB2[j * sb_chunk:],
+                                [D[i * mc:].data_ptr()], N, j * nc, rb, rb, ws_c, wsb_c, stream=stream)
                 ev = torch.cuda.Event()
-                ev.record(s_up)
-                if kind_c == "A":
-                    blocks += [(k, j, ev) for j in have_b]
-                    have_a.append(k)
-                else:
-                    blocks += [(i, k, ev) for i in have_a]
-                    have_b.append(k)
-        done = []
-        for i, j, ev in blocks:
-            stream.wait_event(ev)
-            lib.gemm_gather(ot, mc, nc, Kp, dA2[i * mc:], dB2[j * nc:], dsA2[i * sa_chunk:], dsB2[j * sb_chunk:],
-                            [D[i * mc:].data_ptr()], N, j * nc, rb, rb, ws_c, wsb_c, stream=stream)
-            ev = torch.cuda.Event()
-            ev.record(stream)
-            done.append((i, j, ev))
-        for i, j, ev in done:
-            s_down.wait_event(ev)
-            off = (i * mc * N + j * nc) * esz
-            err = memcpy2d(Dh.data_ptr() + off, N * esz, D.data_ptr() + off, N * esz, nc * esz, mc,
-                           CUDA_MEMCPY_D2H, s_down.cuda_stream)
-            if err != 0:
-                raise RuntimeError(f"cudaMemcpy2DAsync failed: {err}")
-        ev_end = torch.cuda.Event()
-        ev_end.record(s_down)
-        stream.wait_event(ev_end)
+                ev.record(stream)
+                done.append((i, j, ev))
+            for i, j, ev in done:
+                s_down.wait_event(ev)
+                off = (i * mc * N + j * nc) * esz
+                err = memcpy2d(Dh.data_ptr() + off, N * esz, D.data_ptr() + off, N * esz, nc * esz, mc,
+                               CUDA_MEMCPY_D2H, s_down.cuda_stream)
+                if err != 0:
+                    raise RuntimeError(f"cudaMemcpy2DAsync failed: {err}")
+            ev_end = torch.cuda.Event()
+            ev_end.record(s_down)
+            stream.wait_event(ev_end)
 
-    e2e_steps = max(3, min(args.steps, 20))
-    D_dev = D.clone()  # the device-timed result, to compare the end-to-end output with
-    for _ in range(2):
-        e2e_step()
-    torch.cuda.synchronize()
-    bits = torch.int32 if tdt == torch.float32 else torch.int16
-    e2e_same = float((Dh.to(dev).view(bits) == D_dev.view(bits)).float().mean().item())
-    del D_dev
-    if world > 1:
-        dist.barrier()
-    e0 = torch.cuda.Event(enable_timing=True)
-    e1 = torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(e2e_steps):
-        e2e_step()
-    e1.record(stream)
-    torch.cuda.synchronize()
-    e2e_ms = e0.elapsed_time(e1) / e2e_steps
-    if world > 1:
-        t = torch.tensor([e2e_ms], device=dev, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_ms = float(t.item())
-    e2e_value = flops_rank * world / (e2e_ms * 1e-3) / 1e12
-    del pinned, dA2, dB2, dsA2, dsB2, Dh, ws_c
+        e2e_steps = max(3, min(args.steps, 20))
+        D_dev = D.clone()  # the device-timed result, to compare the end-to-end output with
+        for _ in range(2):
+            e2e_step()
+        torch.cuda.synchronize()
+        bits = torch.int32 if tdt == torch.float32 else torch.int16
+        e2e_same = float((Dh.to(dev).view(bits) == D_dev.view(bits)).float().mean().item())
+        del D_dev
+        if world > 1:
+            dist.barrier()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(e2e_steps):
+            e2e_step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        e2e_ms = e0.elapsed_time(e1) / e2e_steps
+        if world > 1:
+            t = torch.tensor([e2e_ms], device=dev, dtype=torch.float64)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            e2e_ms = float(t.item())
+        e2e_value = flops_rank * world / (e2e_ms * 1e-3) / 1e12
+        return {"value": e2e_value, "unit": "TFLOPS", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "ms_per_step": e2e_ms, "bitwise_equal_to_device_run": e2e_same,
+                "path": f"pinned host -> H2D in {ra} row chunks of A and {rc} of B^T (interleaved, with their "
+                        f"scales), overlapped with one C-ABI call (mxfp6_gemm_gather, one destination) per "
+                        f"{mc}x{nc} block of D as soon as its chunks land, overlapped with a pitched D2H "
+                        f"copy per block"}
+
+    e2e = None if args.no_e2e else e2e_leg()
 
     # ---- compact A (the reference's row stride 3K/4 with K % 128 != 0; loader-warp producer) ----
     compact = None
@@ -1025,12 +1033,7 @@ def run_ours(args):
                          "algorithmic_gbs": rf["algorithmic_gbs"],
                          "splitk_workspace_bytes": rf["splitk_workspace_bytes"]},  # partials written, then read
             "cpu_baseline": cpu,
-            "e2e": {"value": e2e_value, "unit": "TFLOPS", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                    "ms_per_step": e2e_ms, "bitwise_equal_to_device_run": e2e_same,
-                    "path": f"pinned host -> H2D in {ra} row chunks of A and {rc} of B^T (interleaved, with their "
-                            f"scales), overlapped with one C-ABI call (mxfp6_gemm_gather, one destination) per "
-                            f"{mc}x{nc} block of D as soon as its chunks land, overlapped with a pitched D2H "
-                            f"copy per block"},
+            "e2e": e2e,
             "gpu_launches": launches,
             "clocks": clk.summary(),
             "device_status": status,
@@ -1058,6 +1061,10 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", choices=sorted(CONFIGS), default="cfg2")
+    ap.add_argument("--shape", default=None,
+                    help="MxNxK:OUT (OUT F32/F16/BF16): time this shape instead of a BASELINE config (E2M3 codes "
+                         "uniform over the 64 codes, E8M0 exponents in [109, 127]); for profiling one route")
+    ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end leg")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-allgather", action="store_true", help="skip the gathers of the config-5 D shards")
     ap.add_argument("--no-strong", action="store_true", help="skip the config-5 column-split leg")
@@ -1079,6 +1086,12 @@ def main():
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3
+    if args.shape:
+        dims, out = args.shape.split(":")
+        M, N, K = (int(x) for x in dims.lower().split("x"))
+        CONFIGS["shape"] = (M, N, K, "codes", (109, 127), out.upper())
+        CONFIG_DESC["shape"] = f"MXFP6 GEMM M={M} N={N} K={K}, {out.upper()} output"
+        args.config = "shape"
     if args.import_only:
         sys.path.insert(0, PKG_DIR)
         import torch

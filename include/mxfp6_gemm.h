@@ -111,11 +111,16 @@ void mxfp6_choose_tile(int M, int N, int Kp, int* out4);
  * and the number of K splits into out[0..2]. FP32 output may split where FP16/BF16 does not. */
 void mxfp6_route(int ot, int M, int N, int Kp, int* out3);
 
-/* How the CTA-pair route cuts the tiles of a partial last wave along N (no counterpart in the
- * reference): 1 = not cut, 2 or 4 = each such tile runs as 2 or 4 sub-tiles of 128 or 64
- * columns side by side. The cut changes only the schedule: every output element sums the same
- * products in the same K order, so results are identical with and without it. */
-int mxfp6_route_tail_parts(int ot, int M, int N, int Kp);
+/* Whether the CTA-pair route runs a stream-K tail (no counterpart in the reference): 1 when its
+ * 256 x 256 tiles do not fill whole waves of CTA pairs, so the last waves' K slabs are shared out
+ * evenly, 0 otherwise. A tile shared by two pairs is summed in one accumulator chain (the first
+ * pair hands its FP32 accumulator to the second through the workspace), so results are identical
+ * to the whole-tile schedule. The workspace then holds 256 KB + 16 bytes per CTA pair; it is in
+ * gemm_workspace_size(). Without it the call runs whole tiles and warns, as for split-K. */
+int mxfp6_route_stream_k(int ot, int M, int N, int Kp);
+
+/* Workspace bytes of the stream-K tail on the current device (256 KB + 16 bytes per CTA pair). */
+size_t mxfp6_stream_k_workspace_bytes(void);
 
 /* K granule (128) and K padded to it. */
 int mxfp6_k_tile(void);
@@ -130,10 +135,11 @@ void mxfp6_gemm_force_tile(int ot, int M, int N, int Kp, int MT, int NT, int spl
                            int A_row_bytes, int B_row_bytes, void* ws, size_t ws_bytes,
                            void* stream);
 
-/* Test hook (no counterpart in the reference): mxfp6_gemm_force_tile plus the CTA pair's cut of
- * a partial last wave (tail_parts 1, or 2 / 4 with MT = NT = 256; see mxfp6_route_tail_parts).
- * mxfp6_gemm_force_tile runs with tail_parts = 1. */
-void mxfp6_gemm_force_route(int ot, int M, int N, int Kp, int MT, int NT, int splits, int tail_parts,
+/* Test hook (no counterpart in the reference): mxfp6_gemm_force_tile plus the CTA pair's stream-K
+ * tail (stream_k 1 with MT = NT = 256 and splits = 1; it takes effect when the tiles do not fill
+ * whole waves, and needs a 256-byte aligned workspace of 256 KB + 16 bytes per CTA pair; see
+ * mxfp6_route_stream_k). mxfp6_gemm_force_tile runs whole tiles (stream_k = 0). */
+void mxfp6_gemm_force_route(int ot, int M, int N, int Kp, int MT, int NT, int splits, int stream_k,
                             const void* dA, const void* dBsh, const uint8_t* dsA, const uint8_t* dsB, void* dD,
                             int A_row_bytes, int B_row_bytes, void* ws, size_t ws_bytes, void* stream);
 

@@ -14,6 +14,7 @@
 #include <cstdio>
 #include <cstring>
 #include <mutex>
+#include <random>
 
 #include "gemm_kernel.cuh"
 #include "gemm_kernel_pair.cuh"
@@ -32,6 +33,14 @@ namespace {
 thread_local int t_last_error = MXFP6_OK;
 thread_local long long t_wait_budget = 0;  // 0: the kernels' default (kern::WAIT_BUDGET)
 std::atomic<uint64_t> g_launches{0};
+
+// Tag of one stream-K launch, written into the workspace's hand-off flags: the flags are never
+// cleared, so a flag counts only when it holds this launch's tag. The high half is drawn once per
+// process, so stale flags from another process's use of the same memory do not match either.
+uint64_t next_sk_epoch() {
+    static std::atomic<uint64_t> counter{((uint64_t)std::random_device{}() << 32) | 1u};
+    return counter.fetch_add(1, std::memory_order_relaxed);
+}
 
 long long wait_budget() {
     return t_wait_budget > 0 ? t_wait_budget : kern::WAIT_BUDGET;
@@ -376,8 +385,11 @@ bool launch_gemm(int M, int N, int Kp, const void* dA, const void* dB, const uin
     set_compact(p, Kp, dA, A_row_bytes);
     p.wait_budget = wait_budget();
     const long long tiles = (long long)p.m_blocks * p.n_blocks * splits;
-    p.tail_first = (int)tiles;
-    p.tail_parts = 1;
+    p.sk_first = (int)tiles;
+    p.sk_total = 0;
+    p.sk_ws = nullptr;
+    p.sk_flags = nullptr;
+    p.sk_epoch = 0;
     const int grid = (int)(tiles < sm_count() ? tiles : sm_count());
     kernel<<<grid, kern::threads_for(AMODE), C::SMEM_BYTES, stream>>>(tmA, tmB, p);
     cudaError_t e = cudaGetLastError();
@@ -391,7 +403,7 @@ bool launch_gemm(int M, int N, int Kp, const void* dA, const void* dB, const uin
 
 template <typename OutT, bool PARTIAL, int AMODE>
 bool launch_pair(int M, int N, int Kp, const void* dA, const void* dB, const uint8_t* sA, const uint8_t* sB,
-                 const kern::DstList& dl, float* ws, int A_row_bytes, int B_row_bytes, int splits, int tail_parts,
+                 const kern::DstList& dl, float* ws, int A_row_bytes, int B_row_bytes, int splits, void* sk_area,
                  cudaStream_t stream) {
     using C = kern::PairConfig<AMODE>;
     auto kernel = kern::gemm_mxfp6_sm100_pair<OutT, PARTIAL, AMODE>;
@@ -409,25 +421,17 @@ bool launch_pair(int M, int N, int Kp, const void* dA, const void* dB, const uin
         set_error(MXFP6_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(attr_err));
         return false;
     }
-    // The persistent pairs take units round-robin: whole tiles, then, when the last wave would be
-    // partial, its tiles cut along N into tail_parts sub-tiles (their B rows through tmBt, whose
-    // box is the sub-tile's half width).
     const int m_blocks = (M + C::BM - 1) / C::BM, n_blocks = (N + C::BN - 1) / C::BN;
     const long long tiles = (long long)m_blocks * n_blocks * splits;
     const int pairs = sm_count() / 2;
-    if (tail_parts != 1 && tail_parts != 2 && tail_parts != 4) tail_parts = 1;
-    const long long rem = tiles % pairs;
-    if (rem == 0) tail_parts = 1;
-    const long long tail_first = tail_parts > 1 ? tiles - rem : tiles;
-    CUtensorMap tmA, tmB, tmSA, tmSB, tmBt;
+    const int clusters = (int)(tiles < pairs ? tiles : pairs);
+    CUtensorMap tmA, tmB, tmSA, tmSB;
     if (!make_a_tmap(AMODE, &tmA, dA, M, Kp, A_row_bytes, 128) || !make_fp6_tmap(&tmB, dB, N, Kp, B_row_bytes, 128) ||
-        !make_sf_tmap(&tmSA, sA, M, Kp, 1, C::SUB) || !make_sf_tmap_x4(&tmSB, sB, N, Kp) ||
-        (tail_parts > 1 && !make_fp6_tmap(&tmBt, dB, N, Kp, B_row_bytes, 128 / tail_parts))) {
+        !make_sf_tmap(&tmSA, sA, M, Kp, 1, C::SUB) || !make_sf_tmap_x4(&tmSB, sB, N, Kp)) {
         set_error(MXFP6_ERR_CUDA, "cuTensorMapEncodeTiled failed for %dx%dx%d (status %d)", M, N, Kp,
                   t_encode_status);
         return false;
     }
-    if (tail_parts == 1) tmBt = tmB;
     kern::Params p;
     p.sfA = sA;
     p.sfB = sB;
@@ -443,10 +447,21 @@ bool launch_pair(int M, int N, int Kp, const void* dA, const void* dB, const uin
     p.out_align32 = (PARTIAL ? aligned(ws, 32) : dst_align32(dl, sizeof(OutT))) ? 1 : 0;
     set_compact(p, Kp, dA, A_row_bytes);
     p.wait_budget = wait_budget();
-    p.tail_first = (int)tail_first;
-    p.tail_parts = tail_parts;
-    const long long units = tail_first + (tiles - tail_first) * tail_parts;
-    const int clusters = (int)(units < pairs ? units : pairs);
+    // Stream-K tail (sk_area non-null, laid out as stream_k_bytes(clusters)): the last waves'
+    // tiles, one whole wave plus the partial one, are shared out by K slabs.
+    p.sk_first = (int)tiles;
+    p.sk_total = 0;
+    p.sk_ws = nullptr;
+    p.sk_flags = nullptr;
+    p.sk_epoch = 0;
+    if (sk_area && !PARTIAL && pair_stream_k(tiles, splits, clusters)) {
+        p.sk_first = (int)((tiles / clusters - 1) * clusters);
+        p.sk_total = (tiles - p.sk_first) * (long long)p.k_slabs;
+        p.sk_ws = static_cast<float*>(sk_area);
+        p.sk_flags = reinterpret_cast<unsigned long long*>(static_cast<uint8_t*>(sk_area) +
+                                                           (size_t)clusters * C::SK_TILE_FLOATS * sizeof(float));
+        p.sk_epoch = next_sk_epoch();
+    }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * clusters, 1, 1);
     cfg.blockDim = dim3(kern::threads_for(AMODE), 1, 1);
@@ -459,7 +474,7 @@ bool launch_pair(int M, int N, int Kp, const void* dA, const void* dB, const uin
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, tmA, tmB, tmSA, tmSB, tmBt, p);
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, tmA, tmB, tmSA, tmSB, p);
     if (e == cudaSuccess) e = cudaGetLastError();
     if (e != cudaSuccess) {
         set_error(MXFP6_ERR_CUDA, "pair GEMM launch failed: %s", cudaGetErrorString(e));
@@ -495,9 +510,11 @@ bool run_route(const Route& r, int M, int N, int Kp, const void* dA, const void*
     const bool part = r.splits > 1;
     bool ok;
     if (r.MT == 256) {
-        ok = part ? launch_pair<float, true, AMODE>(M, N, Kp, dA, dB, sA, sB, dl, wsf, Ar, Br, r.splits, r.tail_parts,
+        // the stream-K hand-off area follows the split-K partials in the workspace
+        void* sk = r.stream_k ? static_cast<uint8_t*>(ws) + (part ? splitk_bytes(M, N, r.splits) : 0) : nullptr;
+        ok = part ? launch_pair<float, true, AMODE>(M, N, Kp, dA, dB, sA, sB, dl, wsf, Ar, Br, r.splits, nullptr,
                                                     stream)
-                  : launch_pair<OutT, false, AMODE>(M, N, Kp, dA, dB, sA, sB, dl, wsf, Ar, Br, 1, r.tail_parts, stream);
+                  : launch_pair<OutT, false, AMODE>(M, N, Kp, dA, dB, sA, sB, dl, wsf, Ar, Br, 1, sk, stream);
     } else if (r.NT == 256) {
         ok = part ? launch_gemm<256, float, true, AMODE>(M, N, Kp, dA, dB, sA, sB, dl, wsf, Ar, Br, r.splits,
                                                            stream)
@@ -550,15 +567,24 @@ void gemm_entry(int ot, int M, int N, int Kp, const void* dA, const void* dB, co
     t_last_error = MXFP6_OK;
     if (!validate(ot, M, N, Kp, dA, dB, sA, sB, dl.p[0], Ar, Br)) return;
     Route r = route_for_out(ot, M, N, Kp);
-    if (r.splits > 1) {
-        const size_t need = splitk_bytes(M, N, r.splits);
-        if (!ws || ws_bytes < need || !aligned(ws, 16)) {
+    const int sms = sm_count();
+    if (r.splits > 1 || r.stream_k) {
+        const size_t need = route_ws_bytes(r, M, N, sms);
+        // the stream-K hand-off area takes 256-bit stores: a 256-byte aligned workspace
+        if (!ws || ws_bytes < need || !aligned(ws, r.stream_k ? 256 : 16)) {
             // Same contract as the reference (src/dispatch.hpp:76-87): correct, only slower.
-            std::fprintf(stderr,
-                         "[mxfp6] split-K skipped for %dx%dx%d: workspace %zu bytes, need %zu — "
-                         "running unsplit (slower). Size it with gemm_workspace_size().\n",
-                         M, N, Kp, ws_bytes, need);
+            if (r.splits > 1)
+                std::fprintf(stderr,
+                             "[mxfp6] split-K skipped for %dx%dx%d: workspace %zu bytes, need %zu — "
+                             "running unsplit (slower). Size it with gemm_workspace_size().\n",
+                             M, N, Kp, ws_bytes, need);
+            else
+                std::fprintf(stderr,
+                             "[mxfp6] stream-K tail skipped for %dx%dx%d: workspace %zu bytes (256-byte aligned), "
+                             "need %zu — running whole tiles (slower). Size it with gemm_workspace_size().\n",
+                             M, N, Kp, ws_bytes, need);
             r.splits = 1;
+            r.stream_k = false;
         }
     }
     // An A the tensor load cannot address (the compact stride 3K/4 with K % 128 != 0) is re-padded
@@ -566,7 +592,7 @@ void gemm_entry(int ot, int M, int N, int Kp, const void* dA, const void* dB, co
     // (gemm_workspace_size with A_row_bytes): one HBM pass, then the tensor-load kernel. Otherwise
     // the kernels' loader warps read it in place (same results, slower).
     if (a_mode(Kp, dA, Ar) == kern::A_CPASYNC && ws && aligned(ws, 256)) {
-        const size_t off = padded_a_offset(r.splits > 1 ? splitk_bytes(M, N, r.splits) : 0);
+        const size_t off = padded_a_offset(route_ws_bytes(r, M, N, sms));
         const int prb = Kp / 4 * 3;
         if (ws_bytes >= off + padded_a_bytes(M, Kp)) {
             uint8_t* pa = static_cast<uint8_t*>(ws) + off;
@@ -633,8 +659,8 @@ TileChoice choose_tile(int M, int N, int Kp) {
 size_t gemm_workspace_size(int M, int N, int Kp) {
     size_t need = 0;
     for (int ot : {MXFP6_OUT_F16, MXFP6_OUT_F32}) {
-        const Route r = route_for_out(ot, M, N, Kp);
-        if (r.splits > 1 && splitk_bytes(M, N, r.splits) > need) need = splitk_bytes(M, N, r.splits);
+        const size_t b = route_ws_bytes(route_for_out(ot, M, N, Kp), M, N, sm_count());
+        if (b > need) need = b;
     }
     return need;
 }
@@ -682,8 +708,7 @@ size_t mxfp6_gemm_workspace_size_a(int M, int N, int Kp, int A_row_bytes) {
 
 size_t mxfp6_gemm_workspace_size_out(int ot, int M, int N, int Kp) {
     if (ot < MXFP6_OUT_F32 || ot > MXFP6_OUT_BF16) return 0;
-    const Route r = route_for_out(ot, M, N, Kp);
-    return r.splits > 1 ? splitk_bytes(M, N, r.splits) : 0;
+    return route_ws_bytes(route_for_out(ot, M, N, Kp), M, N, sm_count());
 }
 
 void mxfp6_choose_tile(int M, int N, int Kp, int* out4) {
@@ -704,8 +729,12 @@ void mxfp6_route(int ot, int M, int N, int Kp, int* out3) {
     out3[2] = r.splits;
 }
 
-int mxfp6_route_tail_parts(int ot, int M, int N, int Kp) {
-    return route_for_out(ot, M, N, Kp).tail_parts;
+int mxfp6_route_stream_k(int ot, int M, int N, int Kp) {
+    return route_for_out(ot, M, N, Kp).stream_k ? 1 : 0;
+}
+
+size_t mxfp6_stream_k_workspace_bytes(void) {
+    return stream_k_bytes(sm_count() / 2);
 }
 
 int mxfp6_k_tile(void) {
@@ -716,12 +745,12 @@ int mxfp6_kpad(int K) {
     return kpad(K);
 }
 
-void mxfp6_gemm_force_route(int ot, int M, int N, int Kp, int MT, int NT, int splits, int tail_parts, const void* dA,
+void mxfp6_gemm_force_route(int ot, int M, int N, int Kp, int MT, int NT, int splits, int stream_k, const void* dA,
                             const void* dBsh, const uint8_t* dsA, const uint8_t* dsB, void* dD, int A_row_bytes,
                             int B_row_bytes, void* ws, size_t ws_bytes, void* stream) {
     t_last_error = MXFP6_OK;
-    if (tail_parts != 1 && (MT != 256 || (tail_parts != 2 && tail_parts != 4))) {
-        set_error(MXFP6_ERR_UNSUPPORTED, "tail cut %d: 1, or 2 or 4 on the 256x256 pair tile", tail_parts);
+    if (stream_k && (MT != 256 || splits != 1)) {
+        set_error(MXFP6_ERR_UNSUPPORTED, "stream-K tail: the 256x256 pair tile without a K split only");
         return;
     }
     if (!validate(ot, M, N, Kp, dA, dBsh, dsA, dsB, dD, A_row_bytes, B_row_bytes)) return;
@@ -736,15 +765,23 @@ void mxfp6_gemm_force_route(int ot, int M, int N, int Kp, int MT, int NT, int sp
                   splitk_bytes(M, N, splits), ws_bytes);
         return;
     }
-    run(ot, Route{MT, NT, splits, tail_parts}, M, N, Kp, dA, dBsh, dsA, dsB, single_dst(dD, N), A_row_bytes,
-        B_row_bytes, ws, static_cast<cudaStream_t>(stream));
+    const size_t sk_need = stream_k_bytes(sm_count() / 2);
+    if (stream_k && (!ws || ws_bytes < sk_need || !aligned(ws, 256))) {
+        set_error(MXFP6_ERR_WORKSPACE, "forced stream-K tail needs %zu workspace bytes (256-byte aligned), got %zu",
+                  sk_need, ws_bytes);
+        return;
+    }
+    Route r{MT, NT, splits};
+    r.stream_k = stream_k != 0;
+    run(ot, r, M, N, Kp, dA, dBsh, dsA, dsB, single_dst(dD, N), A_row_bytes, B_row_bytes, ws,
+        static_cast<cudaStream_t>(stream));
 }
 
 void mxfp6_gemm_force_tile(int ot, int M, int N, int Kp, int MT, int NT, int splits, const void* dA,
                            const void* dBsh, const uint8_t* dsA, const uint8_t* dsB, void* dD,
                            int A_row_bytes, int B_row_bytes, void* ws, size_t ws_bytes,
                            void* stream) {
-    mxfp6_gemm_force_route(ot, M, N, Kp, MT, NT, splits, 1, dA, dBsh, dsA, dsB, dD, A_row_bytes, B_row_bytes, ws,
+    mxfp6_gemm_force_route(ot, M, N, Kp, MT, NT, splits, 0, dA, dBsh, dsA, dsB, dD, A_row_bytes, B_row_bytes, ws,
                            ws_bytes, stream);
 }
 
@@ -755,8 +792,8 @@ void mxfp6_gemm_static_workspace(int ot, int M, int N, int Kp, const void* dA, c
     if (!validate(ot, M, N, Kp, dA, dBsh, dsA, dsB, dD, A_row_bytes, B_row_bytes)) return;
     const Route r = route_for_out(ot, M, N, Kp);
     void* ws = nullptr;
-    if (r.splits > 1) {
-        const size_t need = splitk_bytes(M, N, r.splits);
+    if (r.splits > 1 || r.stream_k) {
+        const size_t need = route_ws_bytes(r, M, N, sm_count());
         if (need > kStaticWorkspaceBytes) {
             set_error(MXFP6_ERR_WORKSPACE,
                       "%dx%dx%d splits K %d ways and needs %zu bytes of split-K scratch; the library's "

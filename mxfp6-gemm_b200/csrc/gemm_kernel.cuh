@@ -98,10 +98,16 @@ struct Params {
     const uint8_t* a_ptr;
     int a_stride, a_valid;
     long long wait_budget;  // cycles a role waits on a barrier before it gives up (WAIT_BUDGET by default)
-    // Pair kernel only: the tiles from tail_first on (the last, partial wave of the persistent
-    // schedule) are each cut along N into tail_parts sub-tiles of 256 / tail_parts columns, so
-    // that more CTA pairs share the last wave. 1 = no cut (tail_first is then the tile count).
-    int tail_first, tail_parts;
+    // Pair kernel only, stream-K tail (gemm_kernel_pair.cuh): tiles [0, sk_first) go to the pairs
+    // round-robin as whole tiles; the K slabs of tiles [sk_first, tiles), sk_total in all, are cut
+    // into one contiguous range per pair. sk_total == 0: no stream-K. A pair that ends inside a
+    // tile hands its FP32 accumulator to the next pair through sk_ws ([pairs][256][256]) and
+    // sk_flags ([pairs][2]: set to sk_epoch when a CTA's 128 rows are written).
+    int sk_first;
+    long long sk_total;
+    float* sk_ws;
+    unsigned long long* sk_flags;
+    unsigned long long sk_epoch;
 };
 
 struct TileCoord {

@@ -20,11 +20,15 @@
 //     down and buffer 1 from its bottom chunk up, so the overlap chunk is read first and the
 //     next tile's MMAs may start as soon as that one chunk has left tensor memory; the rest of
 //     the epilogue runs under the next tile's main loop.
-//   * The persistent pairs take 256 x 256 tiles round-robin. When the last wave would be partial,
-//     its tiles are cut along N into 2 or 4 sub-tiles (128 or 64 columns, all K slabs each) so
-//     that more pairs share it: a sub-tile's MMAs have N = 128 or 64, its B rows come through a
-//     second tensor map with the narrower box, and the MMA reads B's scales from the sub-tile's
-//     own first tensor-memory column. Each output element still sums its K slabs in order.
+//   * The persistent pairs take 256 x 256 tiles round-robin. When the tiles do not fill whole
+//     waves, the last wave and one before it run stream-K: their tiles' K slabs, in tile order,
+//     are cut into one contiguous range per pair, so every pair does the same number of slabs.
+//     A tile that straddles two ranges is summed by one accumulator chain: the first pair's
+//     epilogue hands its FP32 accumulator to the second through the workspace (a flag released
+//     at GPU scope), and the second loads it into tensor memory (tcgen05.st) and continues the
+//     same MMA sequence. Each output element sums its K slabs in order exactly as in the
+//     whole-tile schedule, so results are bit-identical. A pair computes its hand-off first and the
+//     tile it takes over last, so the handing pair finished long before (the wait is bounded).
 //   * No TMA multicast anywhere: each CTA fetches its own operands.
 //   * A compact A (a row stride the 16U6 load cannot address) is copied into the A stages by
 //     four extra loader warps per CTA instead (AMODE = A_CPASYNC, compact_a.cuh).
@@ -60,6 +64,7 @@ struct PairConfig {
     static_assert(TMEM_SFA + 4 <= 512, "tensor memory budget");
     static constexpr int EPI_WARPS = 4;
     static constexpr int BAR_BYTES = 256;
+    static constexpr int SK_TILE_FLOATS = BM * BN;  // one hand-off slot: a 256 x 256 FP32 accumulator
     static constexpr int SMEM_BYTES = 1024 + STAGES * (AB_STAGE + SF_STAGE) + BAR_BYTES + EPI_STG_BYTES;
     static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
 };
@@ -68,33 +73,83 @@ __device__ __forceinline__ void store_cluster_u32(uint32_t cluster_addr, uint32_
     asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(cluster_addr), "r"(v) : "memory");
 }
 
-// One work unit of the pair kernel: a 256 x 256 tile (a split-K segment of one, with splits), or,
-// from p.tail_first on, one of the p.tail_parts sub-tiles that a tile of the last, partial wave
-// is cut into along N (256 / tail_parts columns, all of its K slabs). Cutting along N keeps every
-// output element's K summation whole and in order, so results do not depend on the cut.
+// Work of one CTA pair, in the order the pair processes it. The pair owns its whole tiles
+// (round-robin over tiles [0, sk_first)) and its stream-K range [lo, hi) of the remaining tiles'
+// K slabs (flattened in tile order, k_slabs per tile). It first computes the start segment of the
+// tile its range ends inside and hands that accumulator off, so the next pair finds it ready long
+// before it needs it; then its round-robin tiles; then the whole tiles inside its range; last the
+// end segment of the tile its range begins inside, taken over from the previous pair. A range is
+// at least one tile long, so no tile has a middle segment.
+constexpr int UNIT_WHOLE = 0;      // all K slabs of a tile (or one split-K segment)
+constexpr int UNIT_HAND_OFF = 1;   // a tile's first slabs: the accumulator goes to the next pair
+constexpr int UNIT_TAKE_OVER = 2;  // a tile's last slabs, continuing the previous pair's accumulator
+
 struct PairUnit {
-    TileCoord tc;
-    int n0;     // first output column
-    int width;  // output columns: 256, or 256 / tail_parts
+    TileCoord tc;  // tile coordinates; kb_begin / kb_count are this unit's K slabs
+    int mode;
+    int slot;      // hand-off slot (the handing pair's index)
 };
 
-__device__ __forceinline__ int pair_units(const Params& p) {
+struct PairWork {
+    int n_whole;        // round-robin whole tiles
+    int n;              // units in all
+    long long lo, hi;   // stream-K slab range
+    bool hand_off, take_over;
+    int f0, f1;         // whole tiles inside the range, as indices from sk_first
+};
+
+__device__ __forceinline__ PairWork pair_work(const Params& p, int pair, int npairs) {
+    PairWork w;
     const int tiles = p.m_blocks * p.n_blocks * p.splits;
-    return p.tail_first + (tiles - p.tail_first) * p.tail_parts;
+    const int rr = p.sk_total > 0 ? p.sk_first : tiles;
+    w.n_whole = pair < rr ? (rr - pair + npairs - 1) / npairs : 0;
+    w.n = w.n_whole;
+    w.lo = w.hi = 0;
+    w.hand_off = w.take_over = false;
+    w.f0 = w.f1 = 0;
+    if (p.sk_total > 0) {
+        const long long ks = p.k_slabs;
+        w.lo = p.sk_total * pair / npairs;
+        w.hi = p.sk_total * (pair + 1) / npairs;
+        w.hand_off = (w.hi % ks) != 0;
+        w.take_over = (w.lo % ks) != 0;
+        w.f0 = (int)((w.lo + ks - 1) / ks);
+        w.f1 = (int)(w.hi / ks);
+        w.n += (w.hand_off ? 1 : 0) + (w.f1 - w.f0) + (w.take_over ? 1 : 0);
+    }
+    return w;
 }
 
-__device__ __forceinline__ PairUnit decode_unit(int t, const Params& p) {
+__device__ __forceinline__ PairUnit pair_unit(const Params& p, const PairWork& w, int pair, int npairs, int i) {
     PairUnit u;
-    if (t < p.tail_first) {
-        u.tc = decode_tile(t, p);
-        u.width = 256;
-        u.n0 = u.tc.nb * 256;
-    } else {
-        const int v = t - p.tail_first;
-        u.tc = decode_tile(p.tail_first + v / p.tail_parts, p);
-        u.width = 256 / p.tail_parts;
-        u.n0 = u.tc.nb * 256 + (v % p.tail_parts) * u.width;
+    u.mode = UNIT_WHOLE;
+    u.slot = 0;
+    const int ks = p.k_slabs;
+    if (w.hand_off) {
+        if (i == 0) {
+            u.tc = decode_tile(p.sk_first + (int)(w.hi / ks), p);
+            u.tc.kb_begin = 0;
+            u.tc.kb_count = (int)(w.hi % ks);
+            u.mode = UNIT_HAND_OFF;
+            u.slot = pair;
+            return u;
+        }
+        i--;
     }
+    if (i < w.n_whole) {
+        u.tc = decode_tile(pair + i * npairs, p);
+        return u;
+    }
+    const int j = i - w.n_whole;
+    if (j < w.f1 - w.f0) {
+        u.tc = decode_tile(p.sk_first + w.f0 + j, p);
+        return u;
+    }
+    u.tc = decode_tile(p.sk_first + (int)(w.lo / ks), p);
+    u.tc.kb_begin = (int)(w.lo % ks);
+    u.tc.kb_count = ks - u.tc.kb_begin;
+    u.mode = UNIT_TAKE_OVER;
+    u.slot = pair - 1;
     return u;
 }
 
@@ -105,7 +160,7 @@ template <typename OutT, bool PARTIAL, int AMODE = A_TMA>
 __global__ void __launch_bounds__(threads_for(AMODE), 1)
     gemm_mxfp6_sm100_pair(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                           const __grid_constant__ CUtensorMap tmSA, const __grid_constant__ CUtensorMap tmSB,
-                          const __grid_constant__ CUtensorMap tmBt, const Params p) {
+                          const Params p) {
     using C = PairConfig<AMODE>;
     constexpr bool COMPACT = AMODE != A_TMA;
     static_assert(C::SUB == 1, "one 128-deep slab per stage");
@@ -118,14 +173,17 @@ __global__ void __launch_bounds__(threads_for(AMODE), 1)
     const uint32_t sf_base = base + C::STAGES * C::AB_STAGE;
     const uint32_t bar_base = sf_base + C::STAGES * C::SF_STAGE;
     uint8_t* bar_ptr = base_ptr + (bar_base - base);
-    // barriers: full[S], empty[S], acc_full[2], acc_empty[2], ovl_free, drain
+    // barriers: full[S], empty[S], acc_full[2], acc_empty[2], ovl_free, drain, fill, handed
     auto full_bar = [&](int s) { return bar_base + 8u * s; };
     auto empty_bar = [&](int s) { return bar_base + 8u * (C::STAGES + s); };
     const uint32_t acc_full0 = bar_base + 8u * (2 * C::STAGES);
     const uint32_t acc_empty0 = acc_full0 + 16u;
     const uint32_t ovl_free = acc_full0 + 32u;
     const uint32_t drain_bar = acc_full0 + 40u;
-    const int slot_off = 8 * (2 * C::STAGES + 6);
+    const uint32_t fill_bar = acc_full0 + 48u;    // leader: both CTAs loaded a taken-over accumulator
+    const uint32_t handed_bar = acc_full0 + 56u;  // this CTA's epilogue warps stored a hand-off
+    const int slot_off = 8 * (2 * C::STAGES + 8);
+    static_assert(8 * (2 * C::STAGES + 8) + 16 <= C::BAR_BYTES, "barrier area");
     uint8_t* epi_stg = bar_ptr + C::BAR_BYTES;  // EPI_STG_BYTES: output regrouping (several destinations)
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_ptr + slot_off);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(bar_ptr + slot_off + 8);
@@ -156,6 +214,8 @@ __global__ void __launch_bounds__(threads_for(AMODE), 1)
         }
         sm100::mbar_init(ovl_free, 2 * C::EPI_WARPS);
         sm100::mbar_init(drain_bar, 1);
+        sm100::mbar_init(fill_bar, 2 * C::EPI_WARPS);
+        sm100::mbar_init(handed_bar, C::EPI_WARPS);
         *abort_flag = 0;
         sm100::fence_mbar_init();
         sm100::fence_async_shared();
@@ -163,7 +223,6 @@ __global__ void __launch_bounds__(threads_for(AMODE), 1)
         sm100::prefetch_tmap(&tmB);
         sm100::prefetch_tmap(&tmSA);
         sm100::prefetch_tmap(&tmSB);
-        if (p.tail_parts > 1) sm100::prefetch_tmap(&tmBt);
     }
 
     if (warp == 1) {
@@ -176,9 +235,9 @@ __global__ void __launch_bounds__(threads_for(AMODE), 1)
     sm100::tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
 
-    const int total_units = pair_units(p);
     const int cluster_id = blockIdx.x >> 1;
     const int num_clusters = gridDim.x >> 1;
+    const PairWork work = pair_work(p, cluster_id, num_clusters);
     // Abort bookkeeping, read after the roles have finished (see the end of the kernel): the
     // producer's last load per stage and its phase parity, and whether any MMA was issued.
     uint32_t issued_mask = 0, issued_phase = 0;
@@ -190,18 +249,14 @@ __global__ void __launch_bounds__(threads_for(AMODE), 1)
             int stage = 0;
             uint32_t phase = 0;
             bool ok = true;
-            for (int t = cluster_id; t < total_units && ok; t += num_clusters) {
-                const PairUnit u = decode_unit(t, p);
-                if (u.n0 >= p.N) continue;  // a tail sub-tile wholly past N: no work
+            // the leader's barrier counts both CTAs' bytes: A (unless compact), B, scales
+            constexpr uint32_t tx = 2u * ((COMPACT ? 0u : (uint32_t)A_TMA_BYTES) + 128u * (BK * 3 / 4) +
+                                          (uint32_t)C::SF_STAGE);
+            for (int ui = 0; ui < work.n && ok; ui++) {
+                const PairUnit u = pair_unit(p, work, cluster_id, num_clusters, ui);
                 const TileCoord& tc = u.tc;
                 const int a_row = tc.mb * C::BM + 128 * (int)rank;
-                // each CTA holds half of the unit's B^T rows (128 for a full tile)
-                const int half = u.width / 2;
-                const int b_row = u.n0 + half * (int)rank;
-                const CUtensorMap* tmb = u.width == C::BN ? &tmB : &tmBt;
-                // the leader's barrier counts both CTAs' bytes: A (unless compact), B, scales
-                const uint32_t tx = 2u * ((COMPACT ? 0u : (uint32_t)A_TMA_BYTES) + (uint32_t)half * (BK * 3 / 4) +
-                                          (uint32_t)C::SF_STAGE);
+                const int b_row = tc.nb * C::BN + 128 * (int)rank;
                 for (int i = 0; i < tc.kb_count; i++) {
                     if (!sm100::wait_parity_bounded(empty_bar(stage), phase ^ 1u, abort_flag, p.wait_budget)) {
                         if (!*abort_flag) raise(0x1u);
@@ -214,9 +269,8 @@ __global__ void __launch_bounds__(threads_for(AMODE), 1)
                     if (rank == 0) sm100::mbar_arrive_expect_tx(full_bar(stage), tx);
                     const uint32_t a_dst = ab_base + stage * C::AB_STAGE;
                     if (!COMPACT) sm100::tma_load_2d_pair(a_dst, &tmA, fb, kb * BK, a_row);
-                    sm100::tma_load_2d_pair(a_dst + C::A_BYTES, tmb, fb, kb * BK, b_row);
-                    // scale atoms past the last row block read as zero; a sub-tile's scales lie in
-                    // its tile's two B atoms
+                    sm100::tma_load_2d_pair(a_dst + C::A_BYTES, &tmB, fb, kb * BK, b_row);
+                    // scale atoms past the last row block read as zero
                     const uint32_t sf_dst = sf_base + stage * C::SF_STAGE;
                     sm100::tma_load_3d_pair(sf_dst, &tmSA, fb, 0, kb, tc.mb * 2 + (int)rank);
                     sm100::tma_load_4d_pair(sf_dst + C::SFA_BYTES, &tmSB, fb, 0, 0, kb, tc.nb * 2);
@@ -237,20 +291,16 @@ __global__ void __launch_bounds__(threads_for(AMODE), 1)
             int stage = 0;
             uint32_t phase = 0;
             bool ok = true;
-            int local = 0;  // units this pair has computed: selects the accumulator buffer
-            for (int t = cluster_id; t < total_units && ok; t += num_clusters) {
-                const PairUnit u = decode_unit(t, p);
-                if (u.n0 >= p.N) continue;
-                const TileCoord& tc = u.tc;
-                // N = the unit's width; scale id k selects byte k of each scale word
-                uint32_t idesc_k[BK / 32];
-                const uint32_t idesc = sm100::make_idesc_e2m3(C::BM, u.width);
+            constexpr uint32_t idesc = sm100::make_idesc_e2m3(C::BM, C::BN);
+            uint32_t idesc_k[BK / 32];  // scale id k selects byte k of each scale word
 #pragma unroll
-                for (int k = 0; k < BK / 32; k++) idesc_k[k] = sm100::idesc_with_sf_ids(idesc, k, k);
-                // B's scales sit in 8 tensor-memory columns, one per 32 columns of the tile; a
-                // sub-tile starts at its own first column
-                const uint32_t sfb_t = tmem_base + C::TMEM_SFB + (uint32_t)(u.n0 - tc.nb * C::BN) / 32u;
-                const uint32_t sfa_t = tmem_base + C::TMEM_SFA;
+            for (int k = 0; k < BK / 32; k++) idesc_k[k] = sm100::idesc_with_sf_ids(idesc, k, k);
+            const uint32_t sfa_t = tmem_base + C::TMEM_SFA;
+            const uint32_t sfb_t = tmem_base + C::TMEM_SFB;
+            int local = 0;  // units this pair has computed: selects the accumulator buffer
+            for (int ui = 0; ui < work.n && ok; ui++) {
+                const PairUnit u = pair_unit(p, work, cluster_id, num_clusters, ui);
+                const TileCoord& tc = u.tc;
                 const int b = local & 1;
                 const uint32_t d_taddr = tmem_base + (b ? C::BUF1_COL : 0);
                 if (!sm100::wait_parity_bounded(acc_empty0 + 8u * b, ((local >> 1) & 1) ^ 1u, abort_flag,
@@ -262,6 +312,14 @@ __global__ void __launch_bounds__(threads_for(AMODE), 1)
                     ok = false;
                     break;
                 }
+                // A taken-over tile continues the accumulator the epilogue loaded (one per launch)
+                if (u.mode == UNIT_TAKE_OVER && !sm100::wait_parity_bounded(fill_bar, 0, abort_flag, p.wait_budget)) {
+                    if (!*abort_flag) raise(0x2u);
+                    *abort_flag = 1;
+                    ok = false;
+                    break;
+                }
+                const uint32_t acc0 = u.mode == UNIT_TAKE_OVER ? 1u : 0u;
                 sm100::tc_fence_after();
                 // The issuing thread keeps the tensor pipe's short queue fed: it polls the next
                 // slab's barrier without blocking right after issuing the current one, and
@@ -283,7 +341,8 @@ __global__ void __launch_bounds__(threads_for(AMODE), 1)
                     for (int k = 0; k < BK / 32; k++) {
                         const uint32_t sel = (uint32_t)k << 30;
                         sm100::tc_mma_mxf8f6f4_pair(d_taddr, a_desc0 + off16 + 2 * k, b_desc0 + off16 + 2 * k,
-                                                    idesc_k[k], sfa_t | sel, sfb_t | sel, (i > 0 || k > 0) ? 1u : 0u);
+                                                    idesc_k[k], sfa_t | sel, sfb_t | sel,
+                                                    (acc0 || i > 0 || k > 0) ? 1u : 0u);
                     }
                     mma_issued = true;
                     sm100::tc_commit_pair(empty_bar(stage), 0x3);
@@ -304,10 +363,8 @@ __global__ void __launch_bounds__(threads_for(AMODE), 1)
             int stage = 0;
             uint32_t phase = 0;
             bool ok = true;
-            for (int t = cluster_id; t < total_units && ok; t += num_clusters) {
-                const PairUnit u = decode_unit(t, p);
-                if (u.n0 >= p.N) continue;
-                const TileCoord& tc = u.tc;
+            for (int ui = 0; ui < work.n && ok; ui++) {
+                const TileCoord tc = pair_unit(p, work, cluster_id, num_clusters, ui).tc;
                 for (int i = 0; i < tc.kb_count; i++) {
                     if (!sm100::wait_parity_bounded(full_bar(stage), phase, abort_flag, p.wait_budget)) {
                         if (!*abort_flag) raise(0x1u);
@@ -332,10 +389,8 @@ __global__ void __launch_bounds__(threads_for(AMODE), 1)
         int stage = 0;
         uint32_t phase = 0;
         bool ok = true;
-        for (int t = cluster_id; t < total_units && ok; t += num_clusters) {
-            const PairUnit u = decode_unit(t, p);
-            if (u.n0 >= p.N) continue;
-            const TileCoord& tc = u.tc;
+        for (int ui = 0; ui < work.n && ok; ui++) {
+            const TileCoord tc = pair_unit(p, work, cluster_id, num_clusters, ui).tc;
             const int a_row = tc.mb * C::BM + 128 * (int)rank;
             for (int i = 0; i < tc.kb_count; i++) {
                 int got = 1;
@@ -364,13 +419,77 @@ __global__ void __launch_bounds__(threads_for(AMODE), 1)
         const uint32_t t_lane = tmem_base + ((uint32_t)(32 * quarter) << 16);
         const uint32_t leader_acc_empty = sm100::mapa_shared(acc_empty0, 0);
         const uint32_t leader_ovl_free = sm100::mapa_shared(ovl_free, 0);
+        const uint32_t leader_fill = sm100::mapa_shared(fill_bar, 0);
+        // This thread's row within a 256 x 256 tile (hand-off slots are whole tiles, row-major).
+        const int tile_row = 128 * (int)rank + 32 * quarter + lane;
+        // Load the previous pair's accumulator for a taken-over tile into buffer `bb` (this CTA's
+        // 128 rows), once that pair has released it. The chunk buffer `bb` shares with the other
+        // buffer ([224, 256): chunk 7 of buffer 0, chunk 0 of buffer 1) can only be written once
+        // the running unit's epilogue has read it, so the load comes in two parts: FILL_REST (every
+        // other chunk; waits for the flag), then FILL_SHARED, which also reports to the leader's
+        // fill barrier; FILL_ALL does both. Returns false on a timeout (the flag never came).
+        constexpr int FILL_REST = 1, FILL_SHARED = 2, FILL_ALL = 3;
+        auto take_over = [&](const PairUnit& nu, int bb, int part) -> bool {
+            if (part & FILL_REST) {
+                int got = 1;
+                if (lane == 0) {
+                    const unsigned long long* flag = p.sk_flags + 2 * nu.slot + rank;
+                    got = sm100::ld_acquire_gpu_u64(flag) == p.sk_epoch ? 1 : 0;
+                    const long long t0 = clock64();
+                    while (!got && !*abort_flag && clock64() - t0 <= p.wait_budget)
+                        got = sm100::ld_acquire_gpu_u64(flag) == p.sk_epoch ? 1 : 0;
+                }
+                got = __shfl_sync(0xffffffffu, got, 0);
+                if (!got) return false;
+            }
+            const int shared_chunk = bb ? 0 : C::BN / 32 - 1;
+            const float* src = p.sk_ws + (size_t)nu.slot * C::SK_TILE_FLOATS + (size_t)tile_row * C::BN;
+#pragma unroll 1
+            for (int c = 0; c < C::BN / 32; c++) {
+                if (!((c == shared_chunk ? FILL_SHARED : FILL_REST) & part)) continue;
+                uint32_t r[32];
+#pragma unroll
+                for (int q = 0; q < 8; q++) {
+                    const uint4 v = sm100::ld_cg_v4(src + 32 * c + 4 * q);
+                    r[4 * q] = v.x;
+                    r[4 * q + 1] = v.y;
+                    r[4 * q + 2] = v.z;
+                    r[4 * q + 3] = v.w;
+                }
+                sm100::tmem_st_32x32b_x32(t_lane + (bb ? C::BUF1_COL : 0) + 32 * c, r);
+            }
+            sm100::tmem_st_wait();
+            if (part & FILL_SHARED) {
+                sm100::tc_fence_before();
+                __syncwarp();
+                if (lane == 0) sm100::mbar_arrive_cluster(leader_fill);
+            }
+            return true;
+        };
         int local = 0;  // units this pair has computed: selects the accumulator buffer
-        for (int t = cluster_id; t < total_units; t += num_clusters) {
-            const PairUnit u = decode_unit(t, p);
-            if (u.n0 >= p.N) continue;
+        for (int ui = 0; ui < work.n; ui++) {
+            const PairUnit u = pair_unit(p, work, cluster_id, num_clusters, ui);
             const TileCoord& tc = u.tc;
-            const int nchunks = u.width / 32;  // 32-column chunks of this unit's accumulator
             const int b = local & 1;
+            // The unit after this one, when it takes over a tile, gets its accumulator loaded into
+            // the other buffer: all but the shared chunk now, while this unit's MMAs still run (the
+            // other buffer's previous unit is drained), the shared chunk once this unit's epilogue
+            // has read it. After a hand-off, the whole load waits until this pair's own flag is out
+            // (the next pair may be waiting for it).
+            const bool next_takes_over = !PARTIAL && ui + 1 < work.n &&
+                                         pair_unit(p, work, cluster_id, num_clusters, ui + 1).mode == UNIT_TAKE_OVER;
+            const bool hand_off = !PARTIAL && u.mode == UNIT_HAND_OFF;
+            const bool early = next_takes_over && !hand_off;
+            if (early && !take_over(pair_unit(p, work, cluster_id, num_clusters, ui + 1), b ^ 1, FILL_REST)) {
+                if (lane == 0 && !*abort_flag) raise(0x4u);
+                *abort_flag = 1;
+                break;
+            }
+            if (!PARTIAL && u.mode == UNIT_TAKE_OVER && local == 0 && !take_over(u, b, FILL_ALL)) {
+                if (lane == 0 && !*abort_flag) raise(0x4u);
+                *abort_flag = 1;
+                break;
+            }
             // One lane per warp polls the barrier (fewer pollers on shared memory while the main
             // loop runs); the warp then confirms the completed phase without blocking.
             int got = 1;
@@ -384,30 +503,30 @@ __global__ void __launch_bounds__(threads_for(AMODE), 1)
             }
             sm100::mbar_try_wait(acc_full0 + 8u * b, (local >> 1) & 1);
             sm100::tc_fence_after();
-            const int row = tc.mb * C::BM + 128 * (int)rank + 32 * quarter + lane;
-            const int col0 = u.n0;
-            const bool regroup = !PARTIAL && p.dst.n > 1;
+            const int row = tc.mb * C::BM + tile_row;
+            const int col0 = tc.nb * C::BN;
+            const bool regroup = !PARTIAL && !hand_off && p.dst.n > 1;
             uint32_t pend[16];  // FP16/BF16 with several destinations: first chunk of a 64-column pair
 #pragma unroll 1
             for (int j = 0; j < C::BN / 32; j++) {
-                // buffer 0 top-down, buffer 1 bottom-up: the shared chunk [224, 256) goes first.
-                // A sub-tile fills only its first nchunks chunks (an even number, so the chunk
-                // pairs below stay aligned); the shared chunk is still released at j == 0.
+                // buffer 0 top-down, buffer 1 bottom-up: the shared chunk [224, 256) goes first
                 const int c = b ? j : (C::BN / 32 - 1 - j);
                 const uint32_t tcol = (b ? C::BUF1_COL : 0) + 32 * c;
                 uint32_t r[32];
-                if (c < nchunks) {
-                    sm100::tmem_ld_32x32b_x32(t_lane + tcol, r);
-                    sm100::tmem_ld_wait();
-                }
+                sm100::tmem_ld_32x32b_x32(t_lane + tcol, r);
+                sm100::tmem_ld_wait();
                 if (j == 0) {
                     sm100::tc_fence_before();
                     __syncwarp();
                     if (lane == 0) sm100::mbar_arrive_cluster(leader_ovl_free);
+                    if (early) take_over(pair_unit(p, work, cluster_id, num_clusters, ui + 1), b ^ 1, FILL_SHARED);
                 }
-                if (c >= nchunks) continue;
                 const int col = col0 + 32 * c;
-                if (regroup) {
+                if (hand_off) {
+                    // the raw FP32 accumulator, whole tile, for the next pair to continue
+                    store_words<32>(p.sk_ws + (size_t)u.slot * C::SK_TILE_FLOATS + (size_t)tile_row * C::BN + 32 * c, r,
+                                    true);
+                } else if (regroup) {
                     // chunks are processed in pairs (c, c ^ 1) in both orders; col < N is uniform
                     if (col < p.N) {
                         uint8_t* stg = epi_stg + quarter * EPI_STG_WARP;
@@ -441,6 +560,27 @@ __global__ void __launch_bounds__(threads_for(AMODE), 1)
                         convert_chunk<OutT>(r, w);
                         store_chunk_all<OutT>(p.dst, row, col, w, p.out_align32 != 0);
                     }
+                }
+            }
+            if (hand_off) {
+                // Release the hand-off: every warp's stores, then one flag per CTA (128 rows) at
+                // GPU scope for the next pair to acquire.
+                __threadfence();
+                __syncwarp();
+                if (lane == 0) sm100::mbar_arrive(handed_bar);
+                if (warp == 2 && lane == 0) {
+                    if (sm100::wait_parity_bounded(handed_bar, 0, abort_flag, p.wait_budget)) {
+                        __threadfence();
+                        sm100::st_release_gpu_u64(p.sk_flags + 2 * u.slot + rank, p.sk_epoch);
+                    } else if (!*abort_flag) {
+                        raise(0x4u);
+                    }
+                }
+                __syncwarp();
+                if (next_takes_over && !take_over(pair_unit(p, work, cluster_id, num_clusters, ui + 1), b ^ 1, FILL_ALL)) {
+                    if (lane == 0 && !*abort_flag) raise(0x4u);
+                    *abort_flag = 1;
+                    break;
                 }
             }
             sm100::tc_fence_before();

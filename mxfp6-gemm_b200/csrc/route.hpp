@@ -16,9 +16,9 @@
 //           + T_fixed                                      the kernel's start-up beyond the smallest
 //           + T_reduce + (2S + 1) * M*N*4 / HBM  when S > 1   reduce launch, partial write + read, D
 //
-// On the CTA pair a partial last wave is cut along N (pair_tail_parts): each of its tiles becomes
-// 2 or 4 sub-tiles that run side by side, so the last wave costs a fraction of a full one
-// (TAIL_FRACTION, measured) instead of a whole tile's time.
+// On the CTA pair, tiles that do not fill whole waves run with a stream-K tail (pair_stream_k):
+// the slabs of the last waves are shared out evenly, so `waves` is fractional, plus the cost of
+// handing accumulators between pairs (T_HANDOFF). It needs workspace: stream_k_bytes().
 //
 // T_slab is the time one SM (or pair) spends per slab: 256x256 and 128x256 tiles do the same
 // MMA work per SM per slab; their constants reflect how well each keeps the tensor pipe fed
@@ -33,29 +33,32 @@ struct Route {
     int MT;      // tile rows: 256 = CTA pair, 128 = single CTA
     int NT;      // tile columns
     int splits;  // K segments (1 = no split)
-    int tail_parts = 1;  // CTA pair: N-cuts of each tile of a partial last wave (1, 2 or 4)
+    bool stream_k = false;  // CTA pair: stream-K tail (whole tiles do not fill whole waves)
 };
 
 inline size_t splitk_bytes(int M, int N, int splits) {
     return (size_t)splits * (size_t)M * (size_t)N * sizeof(float);
 }
 
-// N-cuts of each tile of the CTA pair's last wave when that wave is partial: the finest cut
-// (64-column sub-tiles) whose sub-tiles all fit in one wave of `slots` pairs, else 128-column
-// sub-tiles, else none. `units` counts 256 x 256 tiles times split segments.
-inline int pair_tail_parts(long long units, long long slots) {
-    if (units <= 0 || slots <= 0) return 1;
-    const long long rem = units % slots;
-    if (rem == 0) return 1;
-    if (rem * 4 <= slots) return 4;
-    if (rem * 2 <= slots) return 2;
-    return 1;
+// Workspace of the pair kernel's stream-K tail on `pairs` CTA pairs: one 256 x 256 FP32
+// accumulator per pair for hand-offs, then two 8-byte flags per pair.
+inline size_t stream_k_bytes(int pairs) {
+    return (size_t)pairs * (256 * 256 * sizeof(float) + 2 * sizeof(unsigned long long));
 }
 
-// Time of a last wave cut into `parts` sub-tiles, as a fraction of a full wave: the sub-tiles
-// still stream all of A's rows, so they are bound by A's loads rather than by the MMAs.
-inline double pair_tail_fraction(int parts) {
-    return parts >= 4 ? 0.45 : (parts == 2 ? 0.6 : 1.0);
+// Workspace a route uses: split-K partials, then the stream-K hand-off area.
+inline size_t route_ws_bytes(const Route& r, int M, int N, int sms) {
+    return (r.splits > 1 ? splitk_bytes(M, N, r.splits) : 0) + (r.stream_k ? stream_k_bytes(sms / 2) : 0);
+}
+
+// The pair kernel runs a stream-K tail when its tiles (no K split) leave the last wave of `slots`
+// pairs at most two thirds full, and there is at least one whole wave, so that every pair's slab
+// range covers at least one tile (a tile is then shared by at most two pairs, in one accumulator
+// chain). Measured on B200 against whole tiles: 2 / 4 / 8 / 16 / 44 tiles in the last wave of 74
+// gained 10 / 4 / 3 / 1 / 3%; 62 of 74 (8192^3) lost 1%: a nearly full wave costs little, and the
+// hand-offs cost a little everywhere.
+inline bool pair_stream_k(long long tiles, int splits, long long slots) {
+    return splits == 1 && slots > 0 && tiles >= slots && tiles % slots != 0 && (tiles % slots) * 3 <= slots * 2;
 }
 
 inline double route_cost_us(int M, int N, int Kp, int MT, int NT, int S, int sms) {
@@ -89,11 +92,12 @@ inline double route_cost_us(int M, int N, int Kp, int MT, int NT, int S, int sms
     const int slabs = Kp / 128;
     const int per = (slabs + S - 1) / S;
     double waves = (double)((units + slots - 1) / slots);
-    if (MT == 256 && units >= slots) {  // the cut's saving is measured behind full waves only
-        const int parts = pair_tail_parts(units, slots);
-        if (parts > 1) waves = (double)(units / slots) + pair_tail_fraction(parts);
+    double t_handoff = 0.0;
+    if (MT == 256 && pair_stream_k(units, S, slots)) {
+        waves = (double)units / (double)slots;
+        t_handoff = 1.5;  // a hand-off store, then the taken-over accumulator's load
     }
-    double t = waves * (per * t_slab + t_tile) + t_fixed;
+    double t = waves * (per * t_slab + t_tile) + t_fixed + t_handoff;
     if (S > 1) t += T_REDUCE_LAUNCH + (2.0 * S + 1.0) * (double)M * N * 4.0 / HBM;
     return t;
 }
@@ -135,8 +139,8 @@ inline Route route_for(int M, int N, int Kp, int sms, int min_splits = 1) {
         }
     }
     if (best.MT == 256) {
-        const long long units = (long long)((M + 255) / 256) * ((N + 255) / 256) * best.splits;
-        best.tail_parts = pair_tail_parts(units, sms / 2 > 0 ? sms / 2 : 1);
+        const long long tiles = (long long)((M + 255) / 256) * ((N + 255) / 256);
+        best.stream_k = pair_stream_k(tiles, best.splits, sms / 2);
     }
     return best;
 }

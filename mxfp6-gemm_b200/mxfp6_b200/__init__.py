@@ -52,7 +52,8 @@ _force_route = _fn("mxfp6_gemm_force_route", None,
                    [C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_void_p,
                     C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_size_t,
                     C.c_void_p])
-_route_tail = _fn("mxfp6_route_tail_parts", C.c_int, [C.c_int, C.c_int, C.c_int, C.c_int])
+_route_sk = _fn("mxfp6_route_stream_k", C.c_int, [C.c_int, C.c_int, C.c_int, C.c_int])
+_sk_bytes = _fn("mxfp6_stream_k_workspace_bytes", C.c_size_t, [])
 _static_ws_gemm = _fn("mxfp6_gemm_static_workspace", None,
                       [C.c_int, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
                        C.c_void_p, C.c_int, C.c_int, C.c_void_p])
@@ -142,11 +143,11 @@ def choose_tile(M: int, N: int, Kp: int) -> TileChoice:
 
 
 def route(ot, M: int, N: int, Kp: int) -> dict:
-    """The route gemm() takes for output type ot: tile, K splits (mxfp6_route) and the CTA pair's
-    N-cut of a partial last wave (mxfp6_route_tail_parts)."""
+    """The route gemm() takes for output type ot: tile, K splits (mxfp6_route) and whether the CTA
+    pair runs a stream-K tail (mxfp6_route_stream_k)."""
     out = (C.c_int * 3)()
     _route(int(ot), M, N, Kp, out)
-    return {"MT": out[0], "NT": out[1], "splits": out[2], "tail_parts": _route_tail(int(ot), M, N, Kp)}
+    return {"MT": out[0], "NT": out[1], "splits": out[2], "stream_k": bool(_route_sk(int(ot), M, N, Kp))}
 
 
 def gemm_workspace_size(M: int, N: int, Kp: int, ot=None) -> int:
@@ -186,12 +187,17 @@ def gemm_force_tile(ot, M, N, Kp, MT, NT, splits, dA, dBsh, dsA, dsB, dD, A_row_
            A_row_bytes, B_row_bytes, _addr(ws), ws_bytes, s)
 
 
-def gemm_force_route(ot, M, N, Kp, MT, NT, splits, tail_parts, dA, dBsh, dsA, dsB, dD, A_row_bytes, B_row_bytes,
+def gemm_force_route(ot, M, N, Kp, MT, NT, splits, stream_k, dA, dBsh, dsA, dsB, dD, A_row_bytes, B_row_bytes,
                      ws=None, ws_bytes=0, stream=None):
-    """Test hook: gemm_force_tile plus the CTA pair's N-cut of a partial last wave (1, 2 or 4)."""
+    """Test hook: gemm_force_tile plus the CTA pair's stream-K tail (stream_k 0 or 1)."""
     s = 0 if stream is None else (stream.cuda_stream if hasattr(stream, "cuda_stream") else _addr(stream))
-    _force_route(int(ot), M, N, Kp, MT, NT, splits, tail_parts, _addr(dA), _addr(dBsh), _addr(dsA), _addr(dsB),
-                 _addr(dD), A_row_bytes, B_row_bytes, _addr(ws), ws_bytes, s)
+    _force_route(int(ot), M, N, Kp, MT, NT, splits, int(bool(stream_k)), _addr(dA), _addr(dBsh), _addr(dsA),
+                 _addr(dsB), _addr(dD), A_row_bytes, B_row_bytes, _addr(ws), ws_bytes, s)
+
+
+def stream_k_bytes() -> int:
+    """Workspace of the CTA pair's stream-K tail on this device (256 KB + 16 bytes per pair)."""
+    return _sk_bytes()
 
 
 def gemm_gather(ot, M, N, Kp, dA, dBsh, dsA, dsB, dDs, ldd, col0, A_row_bytes, B_row_bytes, ws=None, ws_bytes=0,

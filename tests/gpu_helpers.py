@@ -29,7 +29,7 @@ class DeviceOperands:
 
 
 def run_gemm(dev: DeviceOperands, ot, ws_mode="sized", force=None, poison=True, stream=None):
-    """Run the routed GEMM (or a forced route (MT, NT, splits[, tail_parts])); returns D as a torch
+    """Run the routed GEMM (or a forced route (MT, NT, splits[, stream_k])); returns D as a torch
     CPU tensor."""
     o = dev.ops
     D = torch.empty((o.M, o.N), dtype=TORCH_OUT[ot], device=dev.A.device)
@@ -40,6 +40,8 @@ def run_gemm(dev: DeviceOperands, ot, ws_mode="sized", force=None, poison=True, 
         MT, NT, S = force[:3]
         if S > 1:
             wsb = S * o.M * o.N * 4
+        if len(force) > 3 and force[3]:  # stream-K tail
+            wsb = max(wsb, lib.stream_k_bytes())
     elif ws_mode == "sized":
         wsb = lib.gemm_workspace_size(o.M, o.N, o.Kp)
     elif ws_mode == "none":
@@ -54,7 +56,7 @@ def run_gemm(dev: DeviceOperands, ot, ws_mode="sized", force=None, poison=True, 
     elif len(force) == 3:
         lib.gemm_force_tile(ot, o.M, o.N, o.Kp, force[0], force[1], force[2], dev.A, dev.Bt, dev.sA, dev.sB, D,
                             o.row_bytes, o.row_bytes, ws, wsb, stream=stream)
-    else:  # (MT, NT, splits, tail_parts)
+    else:  # (MT, NT, splits, stream_k)
         lib.gemm_force_route(ot, o.M, o.N, o.Kp, force[0], force[1], force[2], force[3], dev.A, dev.Bt, dev.sA,
                              dev.sB, D, o.row_bytes, o.row_bytes, ws, wsb, stream=stream)
     err = lib.last_error()

@@ -122,8 +122,9 @@ def test_unaligned_base_and_stride(lib, oracle, offset, extra):
 
 
 def test_compact_large_bitwise(lib):
-    """Full-size compact A (8192 x 8192 x 8160, K % 128 = 96) on the pair route: bit-identical to
-    the padded tensor-load path (a size-independent check; the oracle is too slow here)."""
+    """Full-size compact A (8192 x 8192 x 8160, K % 128 = 96) on the pair route with its stream-K
+    tail: bit-identical to the padded tensor-load path (a size-independent check; the oracle is
+    too slow here)."""
     M, N, K = 8192, 8192, 8160
     ops, dev = _setup(M, N, K, kind="codes")
     dA, stride = _compact_buffer(ops)

@@ -33,10 +33,11 @@ def _bits(t):
     return t.view(torch.int32) if t.element_size() == 4 else t.view(torch.int16)
 
 
-# shapes routed to 128x128, 128x128 split 16, 128x256, the 256x256 pair, and the pair split 8
+# shapes routed to 128x128, 128x128 split 16, 128x256, the 256x256 pair, the pair split 8, and
+# the pair with a stream-K tail
 @pytest.mark.parametrize("ot", ["F32", "F16", "BF16"])
 @pytest.mark.parametrize("M,N,K", [(640, 768, 1408), (256, 384, 32768), (2048, 2048, 1024), (2048, 2048, 2048),
-                                   (1024, 512, 24576)])
+                                   (1024, 512, 24576), (2304, 2560, 1024)])
 @pytest.mark.parametrize("col0_blocks", [0, 1])
 def test_two_local_destinations(lib, ot, M, N, K, col0_blocks):
     from gpu_helpers import DeviceOperands, run_gemm

@@ -117,23 +117,45 @@ def test_forced_splits(lib, oracle, ot, M, N, K, MT, NT, S):
 
 
 @pytest.mark.parametrize("ot", OUTS)
-@pytest.mark.parametrize("M,N,K,S", [(512, 768, 1024, 1), (384, 640, 960, 1), (2304, 2560, 1024, 1),
-                                     (4096, 3584, 1024, 1), (2048, 1024, 6400, 3), (128, 128, 128, 1)])
-@pytest.mark.parametrize("parts", [2, 4])
-def test_forced_tail_cuts(lib, oracle, ot, M, N, K, S, parts):
-    """The CTA pair's last, partial wave cut along N into 2 or 4 sub-tiles (128 or 64 columns):
-    partial M and N tiles (sub-tiles wholly past N do no work), a last wave after full waves
-    (90 and 224 tiles on 74 pairs), split-K segments, and a single 128 x 128 block. Results
-    match the oracle and are bit for bit those of the uncut schedule."""
+@pytest.mark.parametrize("M,N,K", [(2304, 2560, 1024), (2432, 2688, 256), (4096, 3584, 1024), (2432, 2688, 2048),
+                                   (18944, 256, 512)])
+def test_forced_stream_k(lib, oracle, ot, M, N, K):
+    """The CTA pair's stream-K tail: 90, 110 and 224 tiles on 74 pairs, so each pair's K-slab
+    range starts and ends inside tiles and hands accumulators on (at K = 256, every two or three
+    slabs), partial M and N edge tiles, and 74 tiles (whole waves: no stream-K). Results match
+    the oracle and are bit for bit those of the whole-tile schedule."""
     from gpu_helpers import check, run_gemm, sample_rows
     ops, dev = _setup(M, N, K)
     o = lib.OutType[ot]
-    plain = run_gemm(dev, o, force=(256, 256, S))
-    D = run_gemm(dev, o, force=(256, 256, S, parts))
+    whole = run_gemm(dev, o, force=(256, 256, 1))
+    D = run_gemm(dev, o, force=(256, 256, 1, 1))
     bits = torch.int32 if o == lib.OutType.F32 else torch.int16
-    assert torch.equal(D.view(bits), plain.view(bits))
+    assert torch.equal(D.view(bits), whole.view(bits))
     rows = sample_rows(M, 128) if M * N * ops.Kp > 2**31 else None
-    check(D, _ref(oracle, ops, rows), o, oracle, rows=rows, label=f"{M}x{N}x{K} S={S} tail/{parts}")
+    check(D, _ref(oracle, ops, rows), o, oracle, rows=rows, label=f"{M}x{N}x{K} stream-K")
+
+
+def test_stream_k_repeated_launches_use_fresh_flags(lib):
+    """Hand-off flags are tagged per launch and never cleared: back-to-back launches on one
+    workspace, and a launch after the workspace was filled with stale data, stay bit-identical."""
+    from gpu_helpers import TORCH_OUT
+    ops, dev = _setup(2304, 2560, 512, kind="codes", seed=3)
+    o = lib.OutType.BF16
+    wsb = lib.stream_k_bytes()
+    ws = torch.empty(wsb, dtype=torch.uint8, device="cuda")
+    outs = []
+    for fill in (None, None, 0xFF, 0x00):
+        if fill is not None:
+            ws.fill_(fill)
+        D = torch.empty((ops.M, ops.N), dtype=TORCH_OUT[o], device="cuda")
+        lib.gemm_force_route(o, ops.M, ops.N, ops.Kp, 256, 256, 1, 1, dev.A, dev.Bt, dev.sA, dev.sB, D,
+                             ops.row_bytes, ops.row_bytes, ws, wsb)
+        assert lib.last_error() == lib.OK
+        outs.append(D)
+    torch.cuda.synchronize()
+    assert lib.device_status() == 0
+    for D in outs[1:]:
+        assert torch.equal(D.view(torch.int16), outs[0].view(torch.int16))
 
 
 @pytest.mark.parametrize("M,N,K", [(128, 384, 3072), (256, 384, 32768), (512, 640, 960), (256, 1408, 384),

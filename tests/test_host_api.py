@@ -119,16 +119,27 @@ def test_route_covers_every_shape(lib):
                     if ot == lib.OutType.F16:  # choose_tile reports the FP16/BF16 route
                         assert r["MT"] == t.MT and r["NT"] == t.NT
                     assert 1 <= r["splits"] <= Kp // 128
-                    if r["splits"] > 1:
-                        need = max(need, r["splits"] * M * N * 4)
+                    # the stream-K tail belongs to the CTA pair without a K split, on tiles that do
+                    # not fill whole waves of 74 pairs (and fill at least one)
+                    tiles = -(-M // 256) * -(-N // 256)
+                    assert r["stream_k"] == (r["MT"] == 256 and r["splits"] == 1 and tiles >= 74 and tiles % 74 != 0
+                                             and (tiles % 74) * 3 <= 148)
+                    b = (r["splits"] * M * N * 4 if r["splits"] > 1 else 0) + (lib.stream_k_bytes() if r["stream_k"] else 0)
+                    need = max(need, b)
                 assert ws == need
 
 
 def test_route_examples(lib):
-    # BASELINE shapes: the square and FFN shapes fill the machine unsplit; the narrow deep-K
-    # shape splits; tiny shapes never split.
-    assert lib.gemm_workspace_size(8192, 8192, 8192) == 0
-    assert lib.gemm_workspace_size(4096, 28672, 8192) == 0
+    # BASELINE shapes: the square and FFN shapes fill the machine unsplit; the FFN shape and its
+    # column shards (1792 / 224 / 448 tiles on 74 pairs) and the wide shape run a stream-K tail,
+    # whose hand-off area is their whole workspace; the narrow deep-K shape splits; tiny shapes
+    # never split.
+    assert lib.gemm_workspace_size(8192, 8192, 8192) == 0  # 1024 tiles: the last wave 62/74 full
+    assert lib.gemm_workspace_size(4096, 28672, 8192) == lib.stream_k_bytes() == 74 * (256 * 256 * 4 + 16)
+    for shape in [(4096, 28672, 8192), (4096, 3584, 8192), (4096, 7168, 8192), (2048, 6144, 16128)]:
+        assert lib.route(lib.OutType.BF16, *shape)["stream_k"], shape
+    assert not lib.route(lib.OutType.F16, 8192, 8192, 8192)["stream_k"]
+    assert not lib.route(lib.OutType.F16, 2048, 1024, 105728)["stream_k"]  # split-K instead
     assert lib.gemm_workspace_size(2048, 1024, 105728) > 0
     assert lib.gemm_workspace_size(256, 256, 512) == 0
     assert lib.gemm_workspace_size(128, 128, 128) == 0
