@@ -22,7 +22,8 @@
 //
 // T_slab is the time one SM (or pair) spends per slab: 256x256 and 128x256 tiles do the same
 // MMA work per SM per slab; their constants reflect how well each keeps the tensor pipe fed
-// (measured: the pair sustains more, the narrow tile pays for streaming A at half the work).
+// (measured: the pair sustains a little more over several waves, the narrow tile streams A at
+// half the work per byte).
 // The cheapest candidate wins (a later candidate must win by 3%). gemm_workspace_size() and
 // gemm() both call route_for(), so the workspace a caller sizes always matches what is used.
 #include <cstddef>
@@ -51,14 +52,26 @@ inline size_t route_ws_bytes(const Route& r, int M, int N, int sms) {
     return (r.splits > 1 ? splitk_bytes(M, N, r.splits) : 0) + (r.stream_k ? stream_k_bytes(sms / 2) : 0);
 }
 
-// The pair kernel runs a stream-K tail when its tiles (no K split) leave the last wave of `slots`
-// pairs at most two thirds full, and there is at least one whole wave, so that every pair's slab
-// range covers at least one tile (a tile is then shared by at most two pairs, in one accumulator
-// chain). Measured on B200 against whole tiles: 2 / 4 / 8 / 16 / 44 tiles in the last wave of 74
-// gained 10 / 4 / 3 / 1 / 3%; 62 of 74 (8192^3) lost 1%: a nearly full wave costs little, and the
-// hand-offs cost a little everywhere.
+// The pair kernel can run a stream-K tail when its tiles (no K split) leave the last wave of `slots`
+// pairs partly empty and there is at least one whole wave, so that every pair's slab range covers
+// at least one tile (a tile is then shared by at most two pairs, in one accumulator chain).
 inline bool pair_stream_k(long long tiles, int splits, long long slots) {
-    return splits == 1 && slots > 0 && tiles >= slots && tiles % slots != 0 && (tiles % slots) * 3 <= slots * 2;
+    return splits == 1 && slots > 0 && tiles >= slots && tiles % slots != 0;
+}
+
+// The router takes the tail only where it pays. It costs about as much as 30-35 slabs of a tile
+// wherever it runs (the hand-offs, and the skew it puts between the pairs that share operands),
+// and saves the idle part of the last wave: (1 - last wave's fill) * slabs per tile. Measured on
+// B200 against whole tiles (BF16, L2 flushed and back to back):
+//   last wave 2/74:  16 slabs -18%, 32 +3%, 48 +10%, 64 +10%      (4096 x 3584)
+//   last wave 4/74:  32 slabs -7%, 64 +6%                          (4096 x 7168)
+//   last wave 34/74: 16 slabs -25%, 32 -9%, 48 -4%, 64 -1%, 96 +6% (4096 x 4096)
+//   last wave 44/74: 32 slabs -12%, 64 -5%, 126 +1%                (2048 x 6144)
+// so it runs where that idle part is at least STREAM_K_MIN_SLABS slabs.
+constexpr int STREAM_K_MIN_SLABS = 35;
+inline bool pair_stream_k_pays(long long tiles, int splits, long long slots, int k_slabs) {
+    return pair_stream_k(tiles, splits, slots) &&
+           (slots - tiles % slots) * (long long)k_slabs >= (long long)STREAM_K_MIN_SLABS * slots;
 }
 
 inline double route_cost_us(int M, int N, int Kp, int MT, int NT, int S, int sms) {
@@ -77,7 +90,10 @@ inline double route_cost_us(int M, int N, int Kp, int MT, int NT, int S, int sms
         t_fixed = 2.5;
         per_unit = 2;
     } else if (NT == 256) {
-        t_slab = 0.40;
+        // measured against the pair (back to back, B200): 6% slower at 4096^3 (3.5 waves), level
+        // or faster at one wave (2048x2048x4096: 21.0 against 22.9 us; 1024x4096x16384: 60.1
+        // against 59.9 us)
+        t_slab = 0.32;
         t_tile = 1.0;
         t_fixed = 0.3;
         per_unit = 1;
@@ -93,9 +109,9 @@ inline double route_cost_us(int M, int N, int Kp, int MT, int NT, int S, int sms
     const int per = (slabs + S - 1) / S;
     double waves = (double)((units + slots - 1) / slots);
     double t_handoff = 0.0;
-    if (MT == 256 && pair_stream_k(units, S, slots)) {
+    if (MT == 256 && pair_stream_k_pays(units, S, slots, slabs)) {
         waves = (double)units / (double)slots;
-        t_handoff = 1.5;  // a hand-off store, then the taken-over accumulator's load
+        t_handoff = 30 * t_slab;  // hand-offs and skew: about 30 slabs' worth (measured, above)
     }
     double t = waves * (per * t_slab + t_tile) + t_fixed + t_handoff;
     if (S > 1) t += T_REDUCE_LAUNCH + (2.0 * S + 1.0) * (double)M * N * 4.0 / HBM;
@@ -140,7 +156,7 @@ inline Route route_for(int M, int N, int Kp, int sms, int min_splits = 1) {
     }
     if (best.MT == 256) {
         const long long tiles = (long long)((M + 255) / 256) * ((N + 255) / 256);
-        best.stream_k = pair_stream_k(tiles, best.splits, sms / 2);
+        best.stream_k = pair_stream_k_pays(tiles, best.splits, sms / 2, slabs);
     }
     return best;
 }

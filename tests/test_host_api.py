@@ -120,10 +120,11 @@ def test_route_covers_every_shape(lib):
                         assert r["MT"] == t.MT and r["NT"] == t.NT
                     assert 1 <= r["splits"] <= Kp // 128
                     # the stream-K tail belongs to the CTA pair without a K split, on tiles that do
-                    # not fill whole waves of 74 pairs (and fill at least one)
+                    # not fill whole waves of 74 pairs (and fill at least one), where the idle part
+                    # of the last wave is at least 35 slabs deep
                     tiles = -(-M // 256) * -(-N // 256)
                     assert r["stream_k"] == (r["MT"] == 256 and r["splits"] == 1 and tiles >= 74 and tiles % 74 != 0
-                                             and (tiles % 74) * 3 <= 148)
+                                             and (74 - tiles % 74) * (Kp // 128) >= 35 * 74)
                     b = (r["splits"] * M * N * 4 if r["splits"] > 1 else 0) + (lib.stream_k_bytes() if r["stream_k"] else 0)
                     need = max(need, b)
                 assert ws == need
@@ -140,6 +141,8 @@ def test_route_examples(lib):
         assert lib.route(lib.OutType.BF16, *shape)["stream_k"], shape
     assert not lib.route(lib.OutType.F16, 8192, 8192, 8192)["stream_k"]
     assert not lib.route(lib.OutType.F16, 2048, 1024, 105728)["stream_k"]  # split-K instead
+    # a shallow K: the tail would cost more than the last wave's idle slabs (4096^3: 32 slabs, 34/74)
+    assert not lib.route(lib.OutType.F16, 4096, 4096, 4096)["stream_k"]
     assert lib.gemm_workspace_size(2048, 1024, 105728) > 0
     assert lib.gemm_workspace_size(256, 256, 512) == 0
     assert lib.gemm_workspace_size(128, 128, 128) == 0
