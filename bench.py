@@ -1054,6 +1054,67 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
+ROUTE_SWEEP_SHAPES = [(256, 256, 512, "F32"), (512, 512, 2048, "F16"), (1024, 1024, 4096, "F16"),
+                      (1024, 2048, 8192, "F16"), (2048, 2048, 1024, "F16"), (2048, 2048, 4096, "F16"),
+                      (512, 4096, 8192, "F16"), (4096, 1024, 4096, "F16"), (1024, 4096, 16384, "BF16"),
+                      (2048, 4096, 2048, "BF16"), (4096, 4096, 4096, "F16"), (768, 3072, 4096, "BF16"),
+                      (1024, 1024, 32768, "F16"), (2048, 2048, 16384, "F16")]
+ROUTE_CANDIDATES = [(256, 256, 1, 0), (256, 256, 1, 1), (256, 256, 2, 0), (256, 256, 4, 0), (128, 256, 1, 0),
+                    (128, 256, 2, 0), (128, 128, 1, 0), (128, 128, 2, 0), (128, 128, 4, 0)]
+
+
+def run_route_sweep(reps=15):
+    """Every forced route (tile, K splits, stream-K tail) on a set of shapes, L2 flushed before each
+    launch, median of `reps`; one JSON line per shape with the routed choice and the fastest. The
+    evidence behind the router's cost model (the operand bytes are random: timing only)."""
+    sys.path.insert(0, PKG_DIR)
+    import torch
+
+    import mxfp6_b200 as lib
+    torch.cuda.set_device(0)
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device="cuda")
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+    g = torch.Generator(device="cuda").manual_seed(SEED_A)
+    for M, N, K, out in ROUTE_SWEEP_SHAPES:
+        Kp = kpad(K)
+        rb = Kp * 3 // 4
+        A = torch.randint(0, 256, (M, rb), dtype=torch.uint8, device="cuda", generator=g)
+        B = torch.randint(0, 256, (N, rb), dtype=torch.uint8, device="cuda", generator=g)
+        sA = torch.randint(109, 128, (lib.tiled_scale_bytes(M, Kp),), dtype=torch.uint8, device="cuda", generator=g)
+        sB = torch.randint(109, 128, (lib.tiled_scale_bytes(N, Kp),), dtype=torch.uint8, device="cuda", generator=g)
+        ot = lib.OutType[out]
+        D = torch.empty((M, N), dtype={"F16": torch.float16, "BF16": torch.bfloat16, "F32": torch.float32}[out],
+                        device="cuda")
+        wsb = max(4 * M * N * 4, lib.stream_k_bytes())
+        ws = torch.empty(wsb, dtype=torch.uint8, device="cuda")
+        tiles = -(-M // 256) * -(-N // 256)
+        res = {}
+        for MT, NT, S, sk in ROUTE_CANDIDATES:
+            if S > Kp // 128 or (sk and (tiles < 74 or tiles % 74 == 0)):
+                continue
+            lib.gemm_force_route(ot, M, N, Kp, MT, NT, S, sk, A, B, sA, sB, D, rb, rb, ws, wsb)
+            if lib.last_error() != lib.OK:
+                continue
+            ts = []
+            for r in range(reps):
+                flush.fill_(r & 0xFF)
+                ev[0].record()
+                lib.gemm_force_route(ot, M, N, Kp, MT, NT, S, sk, A, B, sA, sB, D, rb, rb, ws, wsb)
+                ev[1].record()
+                ev[1].synchronize()
+                ts.append(ev[0].elapsed_time(ev[1]) * 1e3)
+            res[f"{MT}x{NT}/S{S}{'/stream_k' if sk else ''}"] = round(statistics.median(ts), 2)
+        if lib.device_status() != 0:
+            raise RuntimeError("a kernel reported a device timeout during the route sweep")
+        r = lib.route(ot, M, N, Kp)
+        chosen = f"{r['MT']}x{r['NT']}/S{r['splits']}{'/stream_k' if r['stream_k'] else ''}"
+        best = min(res, key=res.get)
+        print(json.dumps({"shape": f"{M}x{N}x{K}", "out": out, "routed": chosen, "routed_us": res.get(chosen),
+                          "fastest": best, "fastest_us": res[best], "us": res}), flush=True)
+        del A, B, sA, sB, D, ws
+        torch.cuda.empty_cache()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -1080,6 +1141,8 @@ def main():
                     help="on one GPU, run the N shard one rank of this many holds (strong scaling)")
     ap.add_argument("--import-only", action="store_true",
                     help="only time the device import of the config's B from the reference's layout")
+    ap.add_argument("--route-sweep", action="store_true",
+                    help="time every forced route on a set of shapes (L2 flushed) next to the routed choice")
     ap.add_argument("--vs-cublas", action="store_true",
                     help="also time cuBLASLt's MXFP8 block-scaled GEMM on the same shape (interleaved "
                          "with this library's, then each sustained for about a second with clocks)")
@@ -1092,7 +1155,9 @@ def main():
         CONFIGS["shape"] = (M, N, K, "codes", (109, 127), out.upper())
         CONFIG_DESC["shape"] = f"MXFP6 GEMM M={M} N={N} K={K}, {out.upper()} output"
         args.config = "shape"
-    if args.import_only:
+    if args.route_sweep:
+        run_route_sweep()
+    elif args.import_only:
         sys.path.insert(0, PKG_DIR)
         import torch
 
