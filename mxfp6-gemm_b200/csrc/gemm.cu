@@ -342,6 +342,14 @@ bool make_a_tmap(int amode, CUtensorMap* map, const void* dA, int M, int Kp, int
     return true;
 }
 
+// Programmatic stream serialization: the kernel may start its set-up while the previous kernel in
+// the stream finishes; it waits (griddepcontrol.wait) before touching global memory, so stream
+// order is kept for its inputs and outputs.
+void set_pdl(cudaLaunchAttribute& a) {
+    a.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    a.val.programmaticStreamSerializationAllowed = 1;
+}
+
 template <int BN, typename OutT, bool PARTIAL, int AMODE>
 bool launch_gemm(int M, int N, int Kp, const void* dA, const void* dB, const uint8_t* sA,
                  const uint8_t* sB, const kern::DstList& dl, float* ws, int A_row_bytes, int B_row_bytes,
@@ -391,8 +399,17 @@ bool launch_gemm(int M, int N, int Kp, const void* dA, const void* dB, const uin
     p.sk_flags = nullptr;
     p.sk_epoch = 0;
     const int grid = (int)(tiles < sm_count() ? tiles : sm_count());
-    kernel<<<grid, kern::threads_for(AMODE), C::SMEM_BYTES, stream>>>(tmA, tmB, p);
-    cudaError_t e = cudaGetLastError();
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid, 1, 1);
+    cfg.blockDim = dim3(kern::threads_for(AMODE), 1, 1);
+    cfg.dynamicSmemBytes = C::SMEM_BYTES;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    set_pdl(attr[0]);
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, tmA, tmB, p);
+    if (e == cudaSuccess) e = cudaGetLastError();
     if (e != cudaSuccess) {
         set_error(MXFP6_ERR_CUDA, "GEMM launch failed: %s", cudaGetErrorString(e));
         return false;
@@ -467,13 +484,14 @@ bool launch_pair(int M, int N, int Kp, const void* dA, const void* dB, const uin
     cfg.blockDim = dim3(kern::threads_for(AMODE), 1, 1);
     cfg.dynamicSmemBytes = C::SMEM_BYTES;
     cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = 2;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
+    set_pdl(attr[1]);
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = 2;
     cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, tmA, tmB, tmSA, tmSB, p);
     if (e == cudaSuccess) e = cudaGetLastError();
     if (e != cudaSuccess) {
@@ -491,8 +509,16 @@ bool launch_reduce(const float* ws, const kern::DstList& dl, int M, int N, int s
     long long blocks = (n4 + 255) / 256;
     const long long cap = (long long)sm_count() * 8;
     if (blocks > cap) blocks = cap;
-    kern::reduce_partials<OutT><<<(int)blocks, 256, 0, stream>>>(ws, dl, N, total, splits);
-    cudaError_t e = cudaGetLastError();
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)blocks, 1, 1);
+    cfg.blockDim = dim3(256, 1, 1);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    set_pdl(attr[0]);
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kern::reduce_partials<OutT>, ws, dl, N, total, splits);
+    if (e == cudaSuccess) e = cudaGetLastError();
     if (e != cudaSuccess) {
         set_error(MXFP6_ERR_CUDA, "split-K reduce launch failed: %s", cudaGetErrorString(e));
         return false;

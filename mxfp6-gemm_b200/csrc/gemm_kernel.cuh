@@ -287,6 +287,10 @@ __global__ void __launch_bounds__(threads_for(AMODE), 1)
     __syncthreads();
     sm100::tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
+    // Set-up done (it reads only kernel parameters): the next kernel may start its own, and this
+    // one waits for the previous kernel's memory before its first global access.
+    sm100::griddep_launch_dependents();
+    sm100::griddep_wait();
 
     const int total_tiles = p.m_blocks * p.n_blocks * p.splits;
     // Abort bookkeeping, read after the roles have finished (see the end of the kernel): the
@@ -494,6 +498,8 @@ __global__ void __launch_bounds__(threads_for(AMODE), 1)
 template <typename OutT>
 __global__ void __launch_bounds__(256) reduce_partials(const float* __restrict__ ws, const DstList dl, int N,
                                                        long long total, int S) {
+    sm100::griddep_launch_dependents();
+    sm100::griddep_wait();  // the partials of the GEMM before it
     const long long n4 = total / 4;
     for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n4;
          i += (long long)gridDim.x * blockDim.x) {

@@ -234,6 +234,10 @@ __global__ void __launch_bounds__(threads_for(AMODE), 1)
     sm100::cluster_sync();  // the peer's loads and arrivals target barriers initialised above
     sm100::tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
+    // Set-up done (it reads only kernel parameters): the next kernel may start its own, and this
+    // one waits for the previous kernel's memory before its first global access.
+    sm100::griddep_launch_dependents();
+    sm100::griddep_wait();
 
     const int cluster_id = blockIdx.x >> 1;
     const int num_clusters = gridDim.x >> 1;

@@ -17,6 +17,7 @@
 #include <cstdio>
 
 #include "mxfp6_gemm.h"
+#include "sm100_ptx.cuh"
 
 namespace mxfp6 {
 void note_launch();  // launch counter (gemm.cu)
@@ -169,6 +170,8 @@ __global__ void pad_tail_kernel(int rows, int row_bytes, uint8_t* __restrict__ p
 template <typename U>
 __global__ void __launch_bounds__(256) repad_kernel(const uint8_t* __restrict__ src, int rows, int src_row_bytes,
                                                     int bytes_used, uint8_t* __restrict__ dst, int dst_row_bytes) {
+    sm100::griddep_launch_dependents();
+    sm100::griddep_wait();  // launched with programmatic stream serialization (launch_repad)
     const int row = blockIdx.x;
     if (row >= rows) return;
     const U* s = reinterpret_cast<const U*>(src + (size_t)row * src_row_bytes);
@@ -198,15 +201,23 @@ cudaError_t launch_repad(const uint8_t* src, int rows, int src_row_bytes, int by
                          int dst_row_bytes, cudaStream_t stream) {
     const uintptr_t a = reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(dst) |
                         (uintptr_t)src_row_bytes | (uintptr_t)dst_row_bytes | (uintptr_t)bytes_used;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(rows, 1, 1);
+    cfg.blockDim = dim3(256, 1, 1);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
     if ((a & 15) == 0)
-        repad_kernel<uint4><<<rows, 256, 0, stream>>>(src, rows, src_row_bytes, bytes_used, dst, dst_row_bytes);
-    else if ((a & 7) == 0)
-        repad_kernel<uint2><<<rows, 256, 0, stream>>>(src, rows, src_row_bytes, bytes_used, dst, dst_row_bytes);
-    else if ((a & 3) == 0)
-        repad_kernel<uint32_t><<<rows, 256, 0, stream>>>(src, rows, src_row_bytes, bytes_used, dst, dst_row_bytes);
-    else
-        repad_kernel<uint8_t><<<rows, 256, 0, stream>>>(src, rows, src_row_bytes, bytes_used, dst, dst_row_bytes);
-    return cudaGetLastError();
+        return cudaLaunchKernelEx(&cfg, repad_kernel<uint4>, src, rows, src_row_bytes, bytes_used, dst, dst_row_bytes);
+    if ((a & 7) == 0)
+        return cudaLaunchKernelEx(&cfg, repad_kernel<uint2>, src, rows, src_row_bytes, bytes_used, dst, dst_row_bytes);
+    if ((a & 3) == 0)
+        return cudaLaunchKernelEx(&cfg, repad_kernel<uint32_t>, src, rows, src_row_bytes, bytes_used, dst,
+                                  dst_row_bytes);
+    return cudaLaunchKernelEx(&cfg, repad_kernel<uint8_t>, src, rows, src_row_bytes, bytes_used, dst, dst_row_bytes);
 }
 
 }  // namespace mxfp6

@@ -105,6 +105,22 @@ __device__ __forceinline__ void cp_async_mbar_arrive_noinc(uint32_t bar) {
     asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(bar) : "memory");
 }
 
+// ---- programmatic dependent launch --------------------------------------------------------------
+// The library's kernels are launched with programmatic stream serialization: a kernel may begin
+// while the previous kernel in its stream is still running, and touches global memory only after
+// griddep_wait(), which returns once that kernel has completed and its memory is visible (a no-op
+// for a kernel launched without the attribute). Every kernel of this library waits before its
+// first global access, so stream order holds for whatever kernels precede or follow it.
+
+// Let the next kernel in the stream begin its set-up once every CTA of this grid has issued this
+// (or exited).
+__device__ __forceinline__ void griddep_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void griddep_wait() {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
 // ---- TMA ---------------------------------------------------------------------------------------
 
 __device__ __forceinline__ void prefetch_tmap(const void* tmap) {
