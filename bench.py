@@ -527,8 +527,11 @@ def per_config_leg(lib, torch, dev, stream, flush, steps, warmup, skip):
         D = torch.empty((M, N), dtype=_torch_out(lib, torch, ot), device=dev)
         ws, wsb = workspace(lib, torch, M, N, Kp, ot, dev)
 
+        def call_on(st):
+            lib.gemm(ot, M, N, Kp, A, Bt, sA, sB, D, rb, rb, ws, wsb, stream=st)
+
         def call():
-            lib.gemm(ot, M, N, Kp, A, Bt, sA, sB, D, rb, rb, ws, wsb, stream=stream)
+            call_on(stream)
 
         per = timed_calls(torch, call, steps, warmup, flush, stream)
         err, status = lib.last_error(), lib.device_status()
@@ -537,8 +540,48 @@ def per_config_leg(lib, torch, dev, stream, flush, steps, warmup, skip):
                  "route": lib.route(ot, M, N, Kp), "ms": ms, "best_ms": min(per), "steps": steps,
                  "error": err, "device_status": status}
         entry.update(roofline_fields(M, N, K, Kp, D.element_size(), ms, wsb))
+        if name == "cfg1":
+            entry["back_to_back"] = back_to_back_per_call(torch, call_on, stream)
         out[name] = entry
         del A, sA, Bt, sB, D, ws
+    return out
+
+
+def back_to_back_per_call(torch, call_on, stream, calls=20, reps=4):
+    """Per-call time of `calls` back-to-back calls between two events, best of `reps` (the
+    reference's own convention for its launch-bound floor, tests/test_gemm.cpp:32-52): issued from
+    Python (host enqueue included where it exceeds the device time), and replayed from a CUDA graph
+    of the same calls (device time only; consecutive kernels overlap their set-up through
+    programmatic dependent launch)."""
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    eager = []
+    for _ in range(reps):
+        e0.record(stream)
+        for _ in range(calls):
+            call_on(stream)
+        e1.record(stream)
+        e1.synchronize()
+        eager.append(e0.elapsed_time(e1) * 1e3 / calls)
+    out = {"calls": calls, "eager_us": min(eager)}
+    try:
+        cs = torch.cuda.Stream()  # capture needs a stream other than the legacy default one
+        cs.wait_stream(stream)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=cs):
+            for _ in range(calls):
+                call_on(cs)
+        graph = []
+        with torch.cuda.stream(cs):  # replay() launches on the current stream
+            for _ in range(reps + 1):
+                e0.record(cs)
+                g.replay()
+                e1.record(cs)
+                e1.synchronize()
+                graph.append(e0.elapsed_time(e1) * 1e3 / calls)
+        out["graph_us"] = min(graph[1:])
+        del g
+    except Exception as e:  # capture unavailable: report the eager figure alone
+        out["graph_unavailable"] = repr(e)[:200]
     return out
 
 
