@@ -542,9 +542,34 @@ def per_config_leg(lib, torch, dev, stream, flush, steps, warmup, skip):
         entry.update(roofline_fields(M, N, K, Kp, D.element_size(), ms, wsb))
         if name == "cfg1":
             entry["back_to_back"] = back_to_back_per_call(torch, call_on, stream)
+            entry["back_to_back"].update(cpp_cfg1_per_call())
         out[name] = entry
         del A, sA, Bt, sB, D, ws
     return out
+
+
+def cpp_cfg1_per_call():
+    """Config 1 timed from C++ through the reference's own API (mxfp6::gemm on the legacy default
+    stream, 20 back-to-back calls, best of 4: the reference harness's convention): the C++
+    drop-in caller of the tests, compiled with g++ against the public headers, in its `time` mode."""
+    import re
+    import subprocess
+    import tempfile
+    cuda = os.environ.get("CUDA_HOME", "/usr/local/cuda")
+    lib_dir = os.path.join(PKG_DIR, "lib")
+    with tempfile.TemporaryDirectory() as tmp:
+        exe = os.path.join(tmp, "drop_in_caller")
+        cmd = ["g++", "-std=c++17", "-O2", "-I", os.path.join(ROOT, "include"), "-I", os.path.join(cuda, "include"),
+               os.path.join(ROOT, "tests", "cpp", "drop_in_caller.cpp"), "-o", exe, "-L", lib_dir, "-lmxfp6gemm",
+               f"-Wl,-rpath,{lib_dir}", "-L", os.path.join(cuda, "lib64"), "-lcudart",
+               f"-Wl,-rpath,{os.path.join(cuda, 'lib64')}"]
+        try:
+            subprocess.run(cmd, check=True, capture_output=True, timeout=120)
+            out = subprocess.run([exe, "time"], check=True, capture_output=True, text=True, timeout=120).stdout
+        except (OSError, subprocess.SubprocessError) as e:
+            return {"cpp_unavailable": repr(e)[:200]}
+    m = re.search(r"cfg1 back-to-back from C\+\+: ([0-9.]+) us per call", out)
+    return {"cpp_eager_us": float(m.group(1))} if m else {"cpp_unavailable": out[-200:]}
 
 
 def back_to_back_per_call(torch, call_on, stream, calls=20, reps=4):

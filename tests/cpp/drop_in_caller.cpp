@@ -11,6 +11,9 @@
 //                         argument validation (errors are recorded, nothing is launched)
 //   drop_in_caller gpu    runs the GEMM flow on the current device for every output type, a
 //                         split-K shape and a compact-A shape (K % 128 != 0)
+//   drop_in_caller time   per-call time of the launch-bound BASELINE config 1 (256x256x512, FP32
+//                         out) timed the reference's way: 8 warm-ups, then 20 back-to-back gemm()
+//                         calls on the legacy default stream between two events, best of 4
 // Exit status 0 on success; each failure prints one line.
 #include <cuda_runtime.h>
 
@@ -210,6 +213,65 @@ void run_case(const Shape& s, OutType ot, uint32_t seed) {
     else std::printf("ok   %s: worst error / tolerance %.3f\n", label, worst);
 }
 
+// BASELINE config 1 through the public C++ API, timed as the reference times its launch-bound
+// floor (tests/test_gemm.cpp:32-52): host enqueue and device time of back-to-back calls.
+void time_cfg1() {
+    const int M = 256, N = 256, K = 512, Kp = kpad(K);
+    std::mt19937 rng(5);
+    std::normal_distribution<float> nd(0.0f, 1.0f);
+    std::vector<float> A((size_t)M * Kp), B((size_t)Kp * N);
+    for (float& v : A) v = nd(rng);
+    for (float& v : B) v = 0.05f * nd(rng);
+    QuantizedMatrix Aq = quantize_to_mxfp6(A.data(), M, Kp);
+    QuantizedMatrix Bq = preprocess_B(B.data(), Kp, N);
+    PreshuffledB Bsh = preshuffle_B(Bq);
+    TileChoice tc = choose_tile(M, N, Kp);
+    TiledScale sA = tile_scale(preprocess_scale(Aq.scales.data(), M, Kp), tc.MPW, K_TILE / 64);
+    TiledScale sB = tile_scale(preprocess_scale(Bq.scales.data(), N, Kp), tc.NPW, K_TILE / 64);
+    const size_t wsb = gemm_workspace_size(M, N, Kp);
+    void *dA, *dB, *dD, *ws = nullptr;
+    uint8_t *dsA, *dsB;
+    CUDA_OK(cudaMalloc(&dA, Aq.packed_data.size()));
+    CUDA_OK(cudaMalloc(&dB, Bsh.data.size()));
+    CUDA_OK(cudaMalloc(&dsA, sA.data.size()));
+    CUDA_OK(cudaMalloc(&dsB, sB.data.size()));
+    CUDA_OK(cudaMalloc(&dD, (size_t)M * N * 4));
+    if (wsb) CUDA_OK(cudaMalloc(&ws, wsb));
+    CUDA_OK(cudaMemcpy(dA, Aq.packed_data.data(), Aq.packed_data.size(), cudaMemcpyHostToDevice));
+    CUDA_OK(cudaMemcpy(dB, Bsh.data.data(), Bsh.data.size(), cudaMemcpyHostToDevice));
+    CUDA_OK(cudaMemcpy(dsA, sA.data.data(), sA.data.size(), cudaMemcpyHostToDevice));
+    CUDA_OK(cudaMemcpy(dsB, sB.data.data(), sB.data.size(), cudaMemcpyHostToDevice));
+    auto call = [&] {
+        gemm(OutType::F32, M, N, Kp, dA, dB, dsA, dsB, dD, Aq.packed_row_bytes, Bq.packed_row_bytes, ws, wsb);
+    };
+    for (int i = 0; i < 8; i++) call();
+    CUDA_OK(cudaDeviceSynchronize());
+    cudaEvent_t e0, e1;
+    CUDA_OK(cudaEventCreate(&e0));
+    CUDA_OK(cudaEventCreate(&e1));
+    float best = 1e30f;
+    for (int rep = 0; rep < 4; rep++) {
+        CUDA_OK(cudaEventRecord(e0, 0));
+        for (int i = 0; i < 20; i++) call();
+        CUDA_OK(cudaEventRecord(e1, 0));
+        CUDA_OK(cudaEventSynchronize(e1));
+        float ms = 0.0f;
+        CUDA_OK(cudaEventElapsedTime(&ms, e0, e1));
+        if (ms < best) best = ms;
+    }
+    if (mxfp6_last_error() != MXFP6_OK || mxfp6_device_status() != 0) fail("cfg1 timing calls reported an error");
+    std::printf("cfg1 back-to-back from C++: %.3f us per call (%s, 20 calls, best of 4)\n", best * 1000.0f / 20,
+                "256x256x512 FP32 out");
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+    cudaFree(dA);
+    cudaFree(dB);
+    cudaFree(dsA);
+    cudaFree(dsB);
+    cudaFree(dD);
+    if (ws) cudaFree(ws);
+}
+
 void gpu_checks() {
     int ndev = 0;
     if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0) {
@@ -235,8 +297,10 @@ int main(int argc, char** argv) {
     else if (mode == "gpu") {
         host_checks();
         gpu_checks();
+    } else if (mode == "time") {
+        time_cfg1();
     } else {
-        std::printf("usage: %s host|gpu\n", argv[0]);
+        std::printf("usage: %s host|gpu|time\n", argv[0]);
         return 2;
     }
     std::printf("%s: %d failure(s)\n", mode.c_str(), g_failures);

@@ -2,7 +2,8 @@
 headers (include/mxfp6/*.hpp, include/mxfp6_gemm.h) and linked to libmxfp6gemm.so, as a C++
 user of the reference library would (reference: include/mxfp6/gemm.hpp:25-64,
 tests/test_gemm.cpp:131-201). `host` mode runs without a device; `gpu` mode runs the reference's
-quantise -> preprocess -> gemm flow for every output type, a split-K shape and a compact-A shape.
+quantise -> preprocess -> gemm flow for every output type, a split-K shape and a compact-A shape;
+`time` mode times BASELINE config 1 back to back as the reference's harness does.
 """
 from __future__ import annotations
 
@@ -49,3 +50,18 @@ def test_gpu_mode(caller):
     out = _run(caller, "gpu", 600)
     assert "gpu: 0 failure(s)" in out
     assert out.count("ok   ") == 12, out
+
+
+@pytest.mark.gpu
+def test_time_mode(caller):
+    """The C++ timing of BASELINE config 1 runs and reports a per-call time (no threshold: it is a
+    measurement, not a check)."""
+    import re
+
+    import torch
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    out = _run(caller, "time", 120)
+    m = re.search(r"cfg1 back-to-back from C\+\+: ([0-9.]+) us per call", out)
+    assert m and float(m.group(1)) > 0, out
+    assert "time: 0 failure(s)" in out
