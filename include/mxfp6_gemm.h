@@ -112,8 +112,9 @@ void mxfp6_choose_tile(int M, int N, int Kp, int* out4);
 void mxfp6_route(int ot, int M, int N, int Kp, int* out3);
 
 /* Whether the CTA-pair route runs a stream-K tail (no counterpart in the reference): 1 when its
- * 256 x 256 tiles do not fill whole waves of CTA pairs, so the last waves' K slabs are shared out
- * evenly, 0 otherwise. A tile shared by two pairs is summed in one accumulator chain (the first
+ * 256 x 256 tiles do not fill whole waves of CTA pairs and the idle part of the last wave is deep
+ * enough to repay the hand-offs (at least 35 slabs of 128 K), so the last waves' K slabs are
+ * shared out evenly; 0 otherwise. A tile shared by two pairs is summed in one accumulator chain (the first
  * pair hands its FP32 accumulator to the second through the workspace), so results are identical
  * to the whole-tile schedule. The workspace then holds 256 KB + 16 bytes per CTA pair; it is in
  * gemm_workspace_size(). Without it the call runs whole tiles and warns, as for split-K. */
