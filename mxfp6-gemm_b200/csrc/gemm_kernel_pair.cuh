@@ -21,7 +21,8 @@
 //     next tile's MMAs may start as soon as that one chunk has left tensor memory; the rest of
 //     the epilogue runs under the next tile's main loop.
 //   * The persistent pairs take 256 x 256 tiles round-robin. When the tiles do not fill whole
-//     waves, the last wave and one before it run stream-K: their tiles' K slabs, in tile order,
+//     waves (and the router finds the idle part of the last wave deep enough to repay it, see
+//     route.hpp), the last wave and one before it run stream-K: their tiles' K slabs, in tile order,
 //     are cut into one contiguous range per pair, so every pair does the same number of slabs.
 //     A tile that straddles two ranges is summed by one accumulator chain: the first pair's
 //     epilogue hands its FP32 accumulator to the second through the workspace (a flag released
