@@ -120,6 +120,15 @@ void mxfp6_route(int ot, int M, int N, int Kp, int* out3);
  * gemm_workspace_size(). Without it the call runs whole tiles and warns, as for split-K. */
 int mxfp6_route_stream_k(int ot, int M, int N, int Kp);
 
+/* No counterpart in the reference (its split-K, src/dispatch.hpp:30-59, cuts K into S equal
+ * segments per tile). 1 when the route is a banded split on the CTA pair. With fewer 256 x 256
+ * tiles (T) than CTA pairs (P) and a deep K, each of the first L*T pairs (L = P / T) takes one
+ * long K band of one tile, and the pairs left over take the short bands the rest of K is cut
+ * into, several tiles each, so that no pair idles and the pairs sharing an operand walk K
+ * together. mxfp6_route reports splits = L + the number of short bands; the workspace is
+ * splits*M*N*4 bytes as for split-K, and the reduce adds each element's bands in K order. */
+int mxfp6_route_banded(int ot, int M, int N, int Kp);
+
 /* Workspace bytes of the stream-K tail on the current device (256 KB + 16 bytes per CTA pair). */
 size_t mxfp6_stream_k_workspace_bytes(void);
 
@@ -139,7 +148,9 @@ void mxfp6_gemm_force_tile(int ot, int M, int N, int Kp, int MT, int NT, int spl
 /* Test hook (no counterpart in the reference): mxfp6_gemm_force_tile plus the CTA pair's stream-K
  * tail (stream_k 1 with MT = NT = 256 and splits = 1; it takes effect when the tiles do not fill
  * whole waves, and needs a 256-byte aligned workspace of 256 KB + 16 bytes per CTA pair; see
- * mxfp6_route_stream_k). mxfp6_gemm_force_tile runs whole tiles (stream_k = 0). */
+ * mxfp6_route_stream_k) or banded split (stream_k 2 with MT = NT = 256 and `splits` short bands,
+ * fewer tiles than CTA pairs; the workspace holds (L + splits)*M*N*4 bytes; see
+ * mxfp6_route_banded). mxfp6_gemm_force_tile runs whole tiles (stream_k = 0). */
 void mxfp6_gemm_force_route(int ot, int M, int N, int Kp, int MT, int NT, int splits, int stream_k,
                             const void* dA, const void* dBsh, const uint8_t* dsA, const uint8_t* dsB, void* dD,
                             int A_row_bytes, int B_row_bytes, void* ws, size_t ws_bytes, void* stream);

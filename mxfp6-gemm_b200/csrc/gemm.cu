@@ -398,6 +398,7 @@ bool launch_gemm(int M, int N, int Kp, const void* dA, const void* dB, const uin
     p.sk_ws = nullptr;
     p.sk_flags = nullptr;
     p.sk_epoch = 0;
+    p.band_L = p.band_a = p.band_n = 0;
     const int grid = (int)(tiles < sm_count() ? tiles : sm_count());
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid, 1, 1);
@@ -421,7 +422,7 @@ bool launch_gemm(int M, int N, int Kp, const void* dA, const void* dB, const uin
 template <typename OutT, bool PARTIAL, int AMODE>
 bool launch_pair(int M, int N, int Kp, const void* dA, const void* dB, const uint8_t* sA, const uint8_t* sB,
                  const kern::DstList& dl, float* ws, int A_row_bytes, int B_row_bytes, int splits, void* sk_area,
-                 cudaStream_t stream) {
+                 cudaStream_t stream, const BandedSplit* band = nullptr) {
     using C = kern::PairConfig<AMODE>;
     auto kernel = kern::gemm_mxfp6_sm100_pair<OutT, PARTIAL, AMODE>;
     static std::once_flag attr_once[kMaxDevices];
@@ -441,7 +442,9 @@ bool launch_pair(int M, int N, int Kp, const void* dA, const void* dB, const uin
     const int m_blocks = (M + C::BM - 1) / C::BM, n_blocks = (N + C::BN - 1) / C::BN;
     const long long tiles = (long long)m_blocks * n_blocks * splits;
     const int pairs = sm_count() / 2;
-    const int clusters = (int)(tiles < pairs ? tiles : pairs);
+    // a banded split (partial mode) keeps every pair busy
+    const bool banded = PARTIAL && band && band->L > 0;
+    const int clusters = banded ? pairs : (int)(tiles < pairs ? tiles : pairs);
     CUtensorMap tmA, tmB, tmSA, tmSB;
     if (!make_a_tmap(AMODE, &tmA, dA, M, Kp, A_row_bytes, 128) || !make_fp6_tmap(&tmB, dB, N, Kp, B_row_bytes, 128) ||
         !make_sf_tmap(&tmSA, sA, M, Kp, 1, C::SUB) || !make_sf_tmap_x4(&tmSB, sB, N, Kp)) {
@@ -479,6 +482,9 @@ bool launch_pair(int M, int N, int Kp, const void* dA, const void* dB, const uin
                                                            (size_t)clusters * C::SK_TILE_FLOATS * sizeof(float));
         p.sk_epoch = next_sk_epoch();
     }
+    p.band_L = banded ? band->L : 0;
+    p.band_a = banded ? band->a : 0;
+    p.band_n = banded ? band->n : 0;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * clusters, 1, 1);
     cfg.blockDim = dim3(kern::threads_for(AMODE), 1, 1);
@@ -538,8 +544,14 @@ bool run_route(const Route& r, int M, int N, int Kp, const void* dA, const void*
     if (r.MT == 256) {
         // the stream-K hand-off area follows the split-K partials in the workspace
         void* sk = r.stream_k ? static_cast<uint8_t*>(ws) + (part ? splitk_bytes(M, N, r.splits) : 0) : nullptr;
+        BandedSplit band;
+        if (r.banded) {
+            const long long tiles = (long long)((M + 255) / 256) * ((N + 255) / 256);
+            const int L = (int)((sm_count() / 2) / tiles);
+            band = banded_split(tiles, sm_count() / 2, Kp / K_TILE, r.splits - L);
+        }
         ok = part ? launch_pair<float, true, AMODE>(M, N, Kp, dA, dB, sA, sB, dl, wsf, Ar, Br, r.splits, nullptr,
-                                                    stream)
+                                                    stream, r.banded ? &band : nullptr)
                   : launch_pair<OutT, false, AMODE>(M, N, Kp, dA, dB, sA, sB, dl, wsf, Ar, Br, 1, sk, stream);
     } else if (r.NT == 256) {
         ok = part ? launch_gemm<256, float, true, AMODE>(M, N, Kp, dA, dB, sA, sB, dl, wsf, Ar, Br, r.splits,
@@ -611,6 +623,7 @@ void gemm_entry(int ot, int M, int N, int Kp, const void* dA, const void* dB, co
                              M, N, Kp, ws_bytes, need);
             r.splits = 1;
             r.stream_k = false;
+            r.banded = false;
         }
     }
     // An A the tensor load cannot address (the compact stride 3K/4 with K % 128 != 0) is re-padded
@@ -759,6 +772,10 @@ int mxfp6_route_stream_k(int ot, int M, int N, int Kp) {
     return route_for_out(ot, M, N, Kp).stream_k ? 1 : 0;
 }
 
+int mxfp6_route_banded(int ot, int M, int N, int Kp) {
+    return route_for_out(ot, M, N, Kp).banded ? 1 : 0;
+}
+
 size_t mxfp6_stream_k_workspace_bytes(void) {
     return stream_k_bytes(sm_count() / 2);
 }
@@ -775,9 +792,25 @@ void mxfp6_gemm_force_route(int ot, int M, int N, int Kp, int MT, int NT, int sp
                             const void* dBsh, const uint8_t* dsA, const uint8_t* dsB, void* dD, int A_row_bytes,
                             int B_row_bytes, void* ws, size_t ws_bytes, void* stream) {
     t_last_error = MXFP6_OK;
-    if (stream_k && (MT != 256 || splits != 1)) {
+    if (stream_k == 1 && (MT != 256 || splits != 1)) {
         set_error(MXFP6_ERR_UNSUPPORTED, "stream-K tail: the 256x256 pair tile without a K split only");
         return;
+    }
+    if (stream_k < 0 || stream_k > 2) {
+        set_error(MXFP6_ERR_UNSUPPORTED, "forced route mode %d (0 plain, 1 stream-K tail, 2 banded split)", stream_k);
+        return;
+    }
+    BandedSplit band;
+    if (stream_k == 2) {
+        // banded split with `splits` short bands
+        const long long tiles = (long long)((M + 255) / 256) * ((N + 255) / 256);
+        band = banded_split(tiles, sm_count() / 2, Kp / K_TILE, splits);
+        if (MT != 256 || NT != 256 || band.L == 0) {
+            set_error(MXFP6_ERR_UNSUPPORTED, "banded split of %dx%dx%d with %d short bands: not available", M, N, Kp,
+                      splits);
+            return;
+        }
+        splits = band.splits();
     }
     if (!validate(ot, M, N, Kp, dA, dBsh, dsA, dsB, dD, A_row_bytes, B_row_bytes)) return;
     const bool tile_ok = (MT == 256 && NT == 256) || (MT == 128 && (NT == 128 || NT == 256));
@@ -792,13 +825,14 @@ void mxfp6_gemm_force_route(int ot, int M, int N, int Kp, int MT, int NT, int sp
         return;
     }
     const size_t sk_need = stream_k_bytes(sm_count() / 2);
-    if (stream_k && (!ws || ws_bytes < sk_need || !aligned(ws, 256))) {
+    if (stream_k == 1 && (!ws || ws_bytes < sk_need || !aligned(ws, 256))) {
         set_error(MXFP6_ERR_WORKSPACE, "forced stream-K tail needs %zu workspace bytes (256-byte aligned), got %zu",
                   sk_need, ws_bytes);
         return;
     }
     Route r{MT, NT, splits};
-    r.stream_k = stream_k != 0;
+    r.stream_k = stream_k == 1;
+    r.banded = stream_k == 2;
     run(ot, r, M, N, Kp, dA, dBsh, dsA, dsB, single_dst(dD, N), A_row_bytes, B_row_bytes, ws,
         static_cast<cudaStream_t>(stream));
 }

@@ -108,6 +108,11 @@ struct Params {
     float* sk_ws;
     unsigned long long* sk_flags;
     unsigned long long sk_epoch;
+    // Pair kernel, partial mode, banded split (band_L > 0): the first band_L * tiles pairs each
+    // take one long band [l * band_a, (l + 1) * band_a) of one tile (partial l); the other pairs
+    // take the band_n short bands that cut [band_L * band_a, k_slabs) evenly, round-robin, band
+    // by band (partial band_L + j).
+    int band_L, band_a, band_n;
 };
 
 struct TileCoord {

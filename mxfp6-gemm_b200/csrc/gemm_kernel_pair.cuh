@@ -99,8 +99,26 @@ struct PairWork {
     int f0, f1;         // whole tiles inside the range, as indices from sk_first
 };
 
+// Banded split: first slab of short band j of band_n over [band_L * band_a, k_slabs).
+__device__ __forceinline__ int band_short_begin(const Params& p, int j) {
+    const int ks = p.k_slabs - p.band_L * p.band_a;
+    return p.band_L * p.band_a + (int)((long long)ks * j / p.band_n);
+}
+
 __device__ __forceinline__ PairWork pair_work(const Params& p, int pair, int npairs) {
     PairWork w;
+    if (p.band_L > 0) {
+        // banded split: one long band per pair on the first band_L * T pairs, short bands
+        // round-robin on the rest (pair_unit)
+        const int T = p.m_blocks * p.n_blocks, longp = p.band_L * T;
+        const int R = npairs - longp, units = p.band_n * T, r = pair - longp;
+        w.n_whole = 0;
+        w.n = pair < longp ? 1 : (R > 0 && r < units ? (units - r + R - 1) / R : 0);
+        w.lo = w.hi = 0;
+        w.hand_off = w.take_over = false;
+        w.f0 = w.f1 = 0;
+        return w;
+    }
     const int tiles = p.m_blocks * p.n_blocks * p.splits;
     const int rr = p.sk_total > 0 ? p.sk_first : tiles;
     w.n_whole = pair < rr ? (rr - pair + npairs - 1) / npairs : 0;
@@ -126,6 +144,22 @@ __device__ __forceinline__ PairUnit pair_unit(const Params& p, const PairWork& w
     u.mode = UNIT_WHOLE;
     u.slot = 0;
     const int ks = p.k_slabs;
+    if (p.band_L > 0) {
+        const int T = p.m_blocks * p.n_blocks, longp = p.band_L * T;
+        if (pair < longp) {
+            u.tc = decode_tile(pair % T, p);
+            u.tc.split = pair / T;
+            u.tc.kb_begin = u.tc.split * p.band_a;
+            u.tc.kb_count = p.band_a;
+        } else {
+            const int v = (pair - longp) + i * (npairs - longp), j = v / T;
+            u.tc = decode_tile(v % T, p);
+            u.tc.split = p.band_L + j;
+            u.tc.kb_begin = band_short_begin(p, j);
+            u.tc.kb_count = band_short_begin(p, j + 1) - u.tc.kb_begin;
+        }
+        return u;
+    }
     if (w.hand_off) {
         if (i == 0) {
             u.tc = decode_tile(p.sk_first + (int)(w.hi / ks), p);

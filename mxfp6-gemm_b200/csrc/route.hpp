@@ -16,6 +16,11 @@
 //           + T_fixed                                      the kernel's start-up beyond the smallest
 //           + T_reduce + (2S + 1) * M*N*4 / HBM  when S > 1   reduce launch, partial write + read, D
 //
+// With fewer 256 x 256 tiles than CTA pairs and a deep K, a banded split is a candidate
+// (BandedSplit): each of the first L*T pairs takes one long K band of one tile, and the pairs
+// left over take the short bands the rest of K is cut into, several tiles each. Every pair then
+// walks K in step with the pairs that share its operands, and the split's partials are reduced
+// in band order as for split-K.
 // On the CTA pair, tiles that do not fill whole waves run with a stream-K tail (pair_stream_k):
 // the slabs of the last waves are shared out evenly, so `waves` is fractional, plus the cost of
 // handing accumulators between pairs (T_HANDOFF). It needs workspace: stream_k_bytes().
@@ -33,9 +38,40 @@ namespace mxfp6 {
 struct Route {
     int MT;      // tile rows: 256 = CTA pair, 128 = single CTA
     int NT;      // tile columns
-    int splits;  // K segments (1 = no split)
+    int splits;  // K segments (1 = no split); banded: long bands + short bands
     bool stream_k = false;  // CTA pair: stream-K tail (whole tiles do not fill whole waves)
+    bool banded = false;    // CTA pair: banded split (BandedSplit below)
 };
+
+// Banded split of T tiles of k_slabs slabs over P CTA pairs (T < P). L = P / T long bands of
+// `a` slabs each, one per pair, on the first L*T pairs; the rest of K (k_slabs - L*a slabs) cut
+// into n short bands, whose n*T units go round-robin, band by band, to the R = P - L*T pairs
+// left, at most q = ceil(n*T / R) each. `a` balances the two: a = q * (k_slabs - L*a) / n.
+// Partial j is band j in K order: long bands 0..L-1, then the short bands.
+struct BandedSplit {
+    int L = 0, a = 0, n = 0;  // L == 0: none
+    int splits() const { return L + n; }
+};
+// First slab and slab count of short band j of n over [L*a, k_slabs).
+inline int band_short_begin(int k_slabs, int L, int a, int n, int j) {
+    const int ks = k_slabs - L * a;
+    return L * a + (int)((long long)ks * j / n);
+}
+inline BandedSplit banded_split(long long tiles, long long pairs, int k_slabs, int n) {
+    BandedSplit b;
+    if (tiles <= 0 || tiles >= pairs || n < 1 || k_slabs < 16) return b;
+    const int L = (int)(pairs / tiles);
+    const long long R = pairs - (long long)L * tiles;
+    if (R <= 0) return b;
+    const long long q = (n * tiles + R - 1) / R;
+    // smallest a with q * ceil((k_slabs - L*a) / n) <= a
+    const long long a = (q * k_slabs + (n + L * q) - 1) / (n + L * q);
+    if (a < 4 || L * a >= k_slabs || (k_slabs - L * a) < n) return b;
+    b.L = L;
+    b.a = (int)a;
+    b.n = n;
+    return b;
+}
 
 inline size_t splitk_bytes(int M, int N, int splits) {
     return (size_t)splits * (size_t)M * (size_t)N * sizeof(float);
@@ -118,6 +154,20 @@ inline double route_cost_us(int M, int N, int Kp, int MT, int NT, int S, int sms
     return t;
 }
 
+// The banded split's cost on the CTA pair: the critical path is one long band (a slabs) or a
+// short-band pair's q units, plus the reduce over L + n partials.
+inline double banded_cost_us(int M, int N, int Kp, int sms, const BandedSplit& b) {
+    const double HBM = 6.5e6, T_REDUCE_LAUNCH = 3.0;
+    const long long tiles = (long long)((M + 255) / 256) * ((N + 255) / 256);
+    const int slabs = Kp / 128;
+    const long long R = sms / 2 - (long long)b.L * tiles;
+    const long long q = (b.n * tiles + R - 1) / R;
+    const int c = (slabs - b.L * b.a + b.n - 1) / b.n;
+    const double path = (double)(b.a > q * c ? b.a : q * c);
+    const int S = b.splits();
+    return path * 0.30 + 0.3 * (double)q + 2.5 + T_REDUCE_LAUNCH + (2.0 * S + 1.0) * (double)M * N * 4.0 / HBM;
+}
+
 // The tensor core's FP32 accumulation loses precision in proportion to the number of K blocks
 // folded into one accumulator (measured: 3.5e-5 max-norm relative error against an exact sum at
 // K = 105728, 1.8e-5 / 1.0e-5 / 0.5e-5 with 2 / 4 / 8 split segments). For FP32 output the route
@@ -154,10 +204,21 @@ inline Route route_for(int M, int N, int Kp, int sms, int min_splits = 1) {
             }
         }
     }
-    if (best.MT == 256) {
-        const long long tiles = (long long)((M + 255) / 256) * ((N + 255) / 256);
-        best.stream_k = pair_stream_k_pays(tiles, best.splits, sms / 2, slabs);
+    const long long tiles = (long long)((M + 255) / 256) * ((N + 255) / 256);
+    if (min_splits == 1 && sms >= 2) {
+        for (int n = 1; n <= 3; n++) {
+            const BandedSplit b = banded_split(tiles, sms / 2, slabs, n);
+            if (b.L == 0) continue;
+            const double t = banded_cost_us(M, N, Kp, sms, b);
+            if (t < best_t * 0.97) {
+                best_t = t;
+                best = Route{256, 256, b.splits()};
+                best.banded = true;
+            }
+        }
+        if (best.banded) return best;
     }
+    if (best.MT == 256) best.stream_k = pair_stream_k_pays(tiles, best.splits, sms / 2, slabs);
     return best;
 }
 

@@ -53,6 +53,7 @@ _force_route = _fn("mxfp6_gemm_force_route", None,
                     C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_size_t,
                     C.c_void_p])
 _route_sk = _fn("mxfp6_route_stream_k", C.c_int, [C.c_int, C.c_int, C.c_int, C.c_int])
+_route_band = _fn("mxfp6_route_banded", C.c_int, [C.c_int, C.c_int, C.c_int, C.c_int])
 _sk_bytes = _fn("mxfp6_stream_k_workspace_bytes", C.c_size_t, [])
 _static_ws_gemm = _fn("mxfp6_gemm_static_workspace", None,
                       [C.c_int, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
@@ -143,11 +144,13 @@ def choose_tile(M: int, N: int, Kp: int) -> TileChoice:
 
 
 def route(ot, M: int, N: int, Kp: int) -> dict:
-    """The route gemm() takes for output type ot: tile, K splits (mxfp6_route) and whether the CTA
-    pair runs a stream-K tail (mxfp6_route_stream_k)."""
+    """The route gemm() takes for output type ot: tile, K splits (mxfp6_route), whether the CTA
+    pair runs a stream-K tail (mxfp6_route_stream_k) and whether its split is banded
+    (mxfp6_route_banded)."""
     out = (C.c_int * 3)()
     _route(int(ot), M, N, Kp, out)
-    return {"MT": out[0], "NT": out[1], "splits": out[2], "stream_k": bool(_route_sk(int(ot), M, N, Kp))}
+    return {"MT": out[0], "NT": out[1], "splits": out[2], "stream_k": bool(_route_sk(int(ot), M, N, Kp)),
+            "banded": bool(_route_band(int(ot), M, N, Kp))}
 
 
 def gemm_workspace_size(M: int, N: int, Kp: int, ot=None) -> int:
@@ -189,9 +192,10 @@ def gemm_force_tile(ot, M, N, Kp, MT, NT, splits, dA, dBsh, dsA, dsB, dD, A_row_
 
 def gemm_force_route(ot, M, N, Kp, MT, NT, splits, stream_k, dA, dBsh, dsA, dsB, dD, A_row_bytes, B_row_bytes,
                      ws=None, ws_bytes=0, stream=None):
-    """Test hook: gemm_force_tile plus the CTA pair's stream-K tail (stream_k 0 or 1)."""
+    """Test hook: gemm_force_tile plus the CTA pair's stream-K tail (stream_k 1) or banded split
+    (stream_k 2, with `splits` short bands)."""
     s = 0 if stream is None else (stream.cuda_stream if hasattr(stream, "cuda_stream") else _addr(stream))
-    _force_route(int(ot), M, N, Kp, MT, NT, splits, int(bool(stream_k)), _addr(dA), _addr(dBsh), _addr(dsA),
+    _force_route(int(ot), M, N, Kp, MT, NT, splits, int(stream_k), _addr(dA), _addr(dBsh), _addr(dsA),
                  _addr(dsB), _addr(dD), A_row_bytes, B_row_bytes, _addr(ws), ws_bytes, s)
 
 

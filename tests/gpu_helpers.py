@@ -40,8 +40,10 @@ def run_gemm(dev: DeviceOperands, ot, ws_mode="sized", force=None, poison=True, 
         MT, NT, S = force[:3]
         if S > 1:
             wsb = S * o.M * o.N * 4
-        if len(force) > 3 and force[3]:  # stream-K tail
+        if len(force) > 3 and force[3] == 1:  # stream-K tail
             wsb = max(wsb, lib.stream_k_bytes())
+        if len(force) > 3 and force[3] == 2:  # banded split: long bands plus `S` short bands
+            wsb = max(wsb, (74 // max(1, (-(-o.M // 256)) * (-(-o.N // 256))) + S) * o.M * o.N * 4)
     elif ws_mode == "sized":
         wsb = lib.gemm_workspace_size(o.M, o.N, o.Kp)
     elif ws_mode == "none":

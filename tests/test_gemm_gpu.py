@@ -135,6 +135,25 @@ def test_forced_stream_k(lib, oracle, ot, M, N, K):
     check(D, _ref(oracle, ops, rows), o, oracle, rows=rows, label=f"{M}x{N}x{K} stream-K")
 
 
+@pytest.mark.parametrize("M,N,K,n,ot", [(2048, 1024, 24576, 1, "F16"), (2048, 1024, 24576, 3, "BF16"),
+                                         (1024, 1024, 32768, 2, "F16"), (768, 1280, 12288, 1, "F32"),
+                                         (2304, 1152, 8192, 2, "BF16"), (2304, 1152, 8192, 3, "F32")])
+def test_forced_banded_split(lib, oracle, M, N, K, n, ot):
+    """The CTA pair's banded split: fewer tiles than pairs (32, 16, 15 and 45; L = 2, 4, 4 and 1
+    long bands per tile, partial M and N edge tiles), the first pairs take one long K band each
+    and the rest share `n` short bands; the partials are reduced in band order. Matches the
+    oracle and is bitwise repeatable."""
+    from gpu_helpers import check, run_gemm, sample_rows
+    ops, dev = _setup(M, N, K)
+    o = lib.OutType[ot]
+    D = run_gemm(dev, o, force=(256, 256, n, 2))
+    again = run_gemm(dev, o, force=(256, 256, n, 2))
+    bits = torch.int32 if o == lib.OutType.F32 else torch.int16
+    assert torch.equal(D.view(bits), again.view(bits))
+    rows = sample_rows(M, 96) if M * N * ops.Kp > 2**31 else None
+    check(D, _ref(oracle, ops, rows), o, oracle, rows=rows, label=f"{M}x{N}x{K} banded n={n}")
+
+
 def test_stream_k_repeated_launches_use_fresh_flags(lib):
     """Hand-off flags are tagged per launch and never cleared: back-to-back launches on one
     workspace, and a launch after the workspace was filled with stale data, stay bit-identical."""

@@ -141,6 +141,12 @@ def test_route_examples(lib):
         assert lib.route(lib.OutType.BF16, *shape)["stream_k"], shape
     assert not lib.route(lib.OutType.F16, 8192, 8192, 8192)["stream_k"]
     assert not lib.route(lib.OutType.F16, 2048, 1024, 105728)["stream_k"]  # split-K instead
+    # 32 tiles on 74 CTA pairs with a deep K: two long bands per tile on 64 pairs, the rest of K on
+    # the other 10 (FP32 keeps its short equal segments)
+    r = lib.route(lib.OutType.F16, 2048, 1024, 105728)
+    assert r["banded"] and r["MT"] == 256 and r["splits"] >= 3
+    assert lib.gemm_workspace_size(2048, 1024, 105728, lib.OutType.F16) == r["splits"] * 2048 * 1024 * 4
+    assert not lib.route(lib.OutType.F32, 2048, 1024, 105728)["banded"]
     # a shallow K: the tail would cost more than the last wave's idle slabs (4096^3: 32 slabs, 34/74)
     assert not lib.route(lib.OutType.F16, 4096, 4096, 4096)["stream_k"]
     assert lib.gemm_workspace_size(2048, 1024, 105728) > 0
