@@ -106,11 +106,13 @@ __device__ __forceinline__ void cp_async_mbar_arrive_noinc(uint32_t bar) {
 }
 
 // ---- programmatic dependent launch --------------------------------------------------------------
-// The library's kernels are launched with programmatic stream serialization: a kernel may begin
-// while the previous kernel in its stream is still running, and touches global memory only after
-// griddep_wait(), which returns once that kernel has completed and its memory is visible (a no-op
-// for a kernel launched without the attribute). Every kernel of this library waits before its
-// first global access, so stream order holds for whatever kernels precede or follow it.
+// The GEMM, split-K reduce and A re-pad kernels are launched with programmatic stream
+// serialization: such a kernel may begin while the previous kernel in its stream is still
+// running, and touches global memory only after griddep_wait(), which returns once that kernel has
+// completed and its memory is visible (a no-op for a kernel launched without the attribute). Each
+// of them waits before its first global access, so stream order holds for whatever kernels precede
+// or follow it. The library's other kernels (quantiser, layout import) launch without the
+// attribute and keep plain stream order.
 
 // Let the next kernel in the stream begin its set-up once every CTA of this grid has issued this
 // (or exited).
