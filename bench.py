@@ -1016,9 +1016,16 @@ def run_ours(args):
         def cstep(w, wb):
             lib.gemm(ot, M, N, Kp, Ac, Btc, sA, sB, D, rbc, rb, w, wb, stream=stream)
 
+        # the reference-sized workspace with the library's re-pad scratch switched off: the loader warps
+        prev = lib.set_repad_scratch(0)
         cper = timed_calls(torch, lambda: cstep(ws, wsb), 10, 3, flush, stream)
+        lib.set_repad_scratch(prev)
         assert lib.last_error() == lib.OK, lib.last_error_string()
         cms = sum(cper) / len(cper)
+        # the same workspace as a drop-in caller has it: A re-padded into the library's scratch
+        sper = timed_calls(torch, lambda: cstep(ws, wsb), 10, 3, flush, stream)
+        assert lib.last_error() == lib.OK, lib.last_error_string()
+        sms_ = sum(sper) / len(sper)
         # with a workspace sized for this A: re-pad into the workspace, then the tensor load
         wsa = lib.gemm_workspace_size_a(M, N, Kp, rbc)
         wsa_t = torch.empty(wsa, dtype=torch.uint8, device=dev)
@@ -1027,15 +1034,21 @@ def run_ours(args):
         rms = sum(rper) / len(rper)
         compact = {"what": f"same GEMM with A in the reference's compact layout (K={Kc}, A_row_bytes={rbc}, "
                            f"not a multiple of 32)",
-                   "in_place": {"how": "workspace from the reference's query: loader-warp cp.async producer",
+                   "in_place": {"how": "workspace from the reference's query, re-pad scratch switched off "
+                                       "(mxfp6_set_repad_scratch(0)): loader-warp cp.async producer",
                                 "ms": cms, "tflops": 2.0 * M * N * Kc / (cms * 1e-3) / 1e12,
                                 "time_ratio_vs_tensor_load": ms / cms},
+                   "scratch": {"how": "workspace from the reference's query (the default): A re-padded into "
+                                      "the library's stream-ordered scratch, then the tensor-load kernel",
+                               "ms": sms_, "tflops": 2.0 * M * N * Kc / (sms_ * 1e-3) / 1e12,
+                               "time_ratio_vs_tensor_load": ms / sms_},
                    "repad": {"how": f"workspace from gemm_workspace_size(M, N, Kp, A_row_bytes) = {wsa} bytes: "
                                     f"A re-padded into it, then the tensor-load kernel",
                              "ms": rms, "tflops": 2.0 * M * N * Kc / (rms * 1e-3) / 1e12,
                              "time_ratio_vs_tensor_load": ms / rms},
                    "device_status": lib.device_status()}
         del Ac, Btc, wsa_t
+        lib.release_repad_scratch()
 
     # ---- the reference's own timing convention (tests/test_gemm.cpp:32-52 of eeezio/mxfp6-gemm):
     # 8 warm-ups, then 20 back-to-back calls between two events, best of 4 repetitions; no L2
@@ -1199,7 +1212,8 @@ def main():
     ap.add_argument("--no-strong", action="store_true", help="skip the config-5 column-split leg")
     ap.add_argument("--no-per-config", action="store_true", help="skip the other BASELINE configs (N=1)")
     ap.add_argument("--with-compact", action="store_true",
-                    help="also time the same GEMM with A in the reference's compact layout (loader warps)")
+                    help="also time the same GEMM with A in the reference's compact layout (loader warps, "
+                         "library re-pad scratch, caller workspace)")
     ap.add_argument("--ref-seconds", type=float, default=10.0, help="target CPU seconds per reference sample")
     ap.add_argument("--e2e-cols", type=int, default=4,
                     help="column chunks of B and D in the end-to-end pipeline (1 = row chunks only)")

@@ -49,8 +49,10 @@ size_t gemm_workspace_size(int M, int N, int Kp);
 // The same for an A of row stride A_row_bytes (no counterpart in the reference): when that stride
 // is not one the tensor load can address (the compact 3K/4 with K % 128 != 0), the size adds room
 // for a padded copy of A, which gemm() then makes (one HBM pass) before running the tensor-load
-// kernel. A workspace sized by the three-argument query still works for such an A: the kernels'
-// loader warps then read it in place, with identical results, at about 0.57 of the speed.
+// kernel. With a workspace sized by the three-argument query, gemm() makes the same copy in
+// scratch from a stream-ordered memory pool of its own when M*N*Kp >= 2^31 (not while the
+// stream captures a graph; mxfp6_set_repad_scratch in mxfp6_gemm.h switches it off), and
+// otherwise the kernels' loader warps read A in place. The results are identical every way.
 size_t gemm_workspace_size(int M, int N, int Kp, int A_row_bytes);
 
 // D[M,N] = A[M,K] * B[K,N]; see the layout notes above. Requirements (checked; a violation

@@ -174,6 +174,28 @@ void mxfp6_gemm_static_workspace(int ot, int M, int N, int Kp, const void* dA, c
 /* Size in bytes of the static split-K array mxfp6_gemm_static_workspace uses. */
 size_t mxfp6_static_workspace_bytes(void);
 
+/* No counterpart in the reference. Re-pad scratch for a compact A (a row stride the tensor
+ * load cannot address: the reference's compact stride 3K/4 with K % 128 != 0). mxfp6_gemm,
+ * mxfp6_gemm_stream and mxfp6_gemm_gather re-pad such an A before the GEMM, which then runs at
+ * about the speed of a padded A. The padded copy goes into the caller's workspace when
+ * mxfp6_gemm_workspace_size_a sized it; otherwise, when M*N*Kp >= 2^31, into scratch that the
+ * library takes, in stream order, from a memory pool of its own on the current device
+ * (M * 0.75*Kp bytes per call, given back in stream order after the GEMM; the pool keeps what it
+ * has mapped, in 32 MiB steps, for later calls). No scratch is taken for smaller GEMMs (there the
+ * extra launch and pool calls cost more than they save), while the stream is capturing a graph,
+ * when it is switched off, or when the allocation fails: the kernels then read A in place
+ * (identical results; on large shapes about half the speed). mxfp6_gemm_static_workspace and the
+ * force hooks never take it.
+ *   mxfp6_set_repad_scratch       1 (default; MXFP6_REPAD_SCRATCH=0 in the environment at load
+ *                                 makes it 0) lets calls take scratch, 0 forbids it; process-wide.
+ *                                 Returns the previous setting.
+ *   mxfp6_repad_scratch_bytes     bytes the pool holds on the current device.
+ *   mxfp6_release_repad_scratch   synchronises the current device and returns the pool's memory
+ *                                 to the driver; 0 or MXFP6_ERR_CUDA. */
+int mxfp6_set_repad_scratch(int enable);
+size_t mxfp6_repad_scratch_bytes(void);
+int mxfp6_release_repad_scratch(void);
+
 /* Status of the last mxfp6_* call on this thread, and a static message for it. */
 int mxfp6_last_error(void);
 const char* mxfp6_last_error_string(void);

@@ -59,6 +59,9 @@ _static_ws_gemm = _fn("mxfp6_gemm_static_workspace", None,
                       [C.c_int, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
                        C.c_void_p, C.c_int, C.c_int, C.c_void_p])
 static_workspace_bytes = _fn("mxfp6_static_workspace_bytes", C.c_size_t, [])
+set_repad_scratch = _fn("mxfp6_set_repad_scratch", C.c_int, [C.c_int])  # returns the previous setting
+repad_scratch_bytes = _fn("mxfp6_repad_scratch_bytes", C.c_size_t, [])
+release_repad_scratch = _fn("mxfp6_release_repad_scratch", C.c_int, [])
 _gather = _fn("mxfp6_gemm_gather", None,
               [C.c_int, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
                C.POINTER(C.c_void_p), C.c_int, C.c_longlong, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_size_t,
