@@ -69,7 +69,7 @@ CFG5_SIGMA = (1.0, 0.02)  # A activation-like N(0, 1), B weight-like N(0, 0.02)
 METRIC = "MXFP6 GEMM TFLOPS (2*M*N*K / device time)"
 L2_FLUSH_BYTES = 256 << 20
 L2_NOTE = "256 MiB buffer written before every timed step (L2 flushed)"
-E2E_ROW_CHUNKS = 8  # row chunks of A (and of D) in the end-to-end step
+E2E_ROW_CHUNKS = 8  # default row chunks of A (and of D) in the end-to-end step
 CUDA_MEMCPY_D2H = 2
 # DRAM bytes (read + write) per launch of the dominant kernel, from one ncu capture of this
 # bench's own command (profiles/gemm_mxfp6_sm100_pair_cfg2.md); None where not captured yet.
@@ -905,22 +905,30 @@ def run_ours(args):
     # ---- end to end through the C ABI with host buffers ----
     def e2e_leg():
         pinned = {k: v.cpu().pin_memory() for k, v in (("A", A), ("Bt", Bt), ("sA", sA), ("sB", sB))}
-        dA2, dB2, dsA2, dsB2 = (torch.empty_like(t) for t in (A, Bt, sA, sB))
-        Dh = torch.empty((M, N), dtype=tdt).pin_memory()
+        # Two sets of device operands and results (and two pinned result buffers), used by
+        # alternate steps, so that one step's uploads can run while the previous step's results
+        # go down. Every step still moves all of its inputs up and all of its result down.
+        sets = []
+        for _ in range(2):
+            sets.append({"A": torch.empty_like(A), "Bt": torch.empty_like(Bt), "sA": torch.empty_like(sA),
+                         "sB": torch.empty_like(sB), "D": torch.empty_like(D),
+                         "Dh": torch.empty((M, N), dtype=tdt).pin_memory(), "computed": None, "down": None})
         h2d = sum(p.numel() * p.element_size() for p in pinned.values())
-        d2h = Dh.numel() * Dh.element_size()
+        d2h = sets[0]["Dh"].numel() * sets[0]["Dh"].element_size()
 
-        # The step's transfers and math overlap in a two-dimensional block pipeline. A is cut into
+        # A step's transfers and math overlap in a two-dimensional block pipeline. A is cut into
         # row chunks and B^T into row chunks (column chunks of B and D). The chunks go up on a copy
         # stream in an order that keeps D blocks coming as early as possible (e2e_upload_order); a
         # first block of D is computable after two chunks. Each block D[i, j] is one call of the
         # library's public entry on the compute stream as soon as A_i and B_j have landed:
         # mxfp6_gemm_gather with one destination (D's row i*mc) writes the block straight into D
         # (row stride N, first column j*nc). Each block goes back on a third stream, as a pitched
-        # copy, as soon as it is computed. Every byte still crosses PCIe inside every step.
+        # copy, as soon as it is computed. Consecutive steps use alternate buffer sets: a step's
+        # uploads wait only until the GEMMs of the step before last (same set) have read their
+        # operands, and its GEMMs until that step's result has gone down.
         s_up = torch.cuda.Stream(dev)
         s_down = torch.cuda.Stream(dev)
-        ra = E2E_ROW_CHUNKS if M % (128 * E2E_ROW_CHUNKS) == 0 else 1
+        ra = args.e2e_rows if args.e2e_rows > 0 and M % (128 * args.e2e_rows) == 0 else 1
         rc = args.e2e_cols if args.e2e_cols > 0 and N % (128 * args.e2e_cols) == 0 else 1
         mc, nc = M // ra, N // rc
         sa_chunk = (mc // 128) * (Kp // 128) * 512  # scale atoms are row-block major
@@ -928,23 +936,22 @@ def run_ours(args):
         ws_c, wsb_c = workspace(lib, torch, mc, nc, Kp, ot, dev)  # a block's own route may split K
         order = e2e_upload_order(ra, rc, mc * rb, nc * rb)
         memcpy2d = cudart_memcpy2d_async()
-        esz = Dh.element_size()
+        esz = sets[0]["Dh"].element_size()
 
-        def e2e_step():
-            ev_start = torch.cuda.Event()
-            ev_start.record(stream)
-            s_up.wait_event(ev_start)
+        def e2e_step(st):
+            if st["computed"] is not None:
+                s_up.wait_event(st["computed"])  # the step before last has read this set's operands
             have_a, have_b, blocks = [], [], []
             with torch.cuda.stream(s_up):
                 for kind_c, k in order:
                     if kind_c == "A":
-                        dA2[k * mc:(k + 1) * mc].copy_(pinned["A"][k * mc:(k + 1) * mc], non_blocking=True)
-                        dsA2[k * sa_chunk:(k + 1) * sa_chunk].copy_(pinned["sA"][k * sa_chunk:(k + 1) * sa_chunk],
-                                                                    non_blocking=True)
+                        st["A"][k * mc:(k + 1) * mc].copy_(pinned["A"][k * mc:(k + 1) * mc], non_blocking=True)
+                        st["sA"][k * sa_chunk:(k + 1) * sa_chunk].copy_(
+                            pinned["sA"][k * sa_chunk:(k + 1) * sa_chunk], non_blocking=True)
                     else:
-                        dB2[k * nc:(k + 1) * nc].copy_(pinned["Bt"][k * nc:(k + 1) * nc], non_blocking=True)
-                        dsB2[k * sb_chunk:(k + 1) * sb_chunk].copy_(pinned["sB"][k * sb_chunk:(k + 1) * sb_chunk],
-                                                                    non_blocking=True)
+                        st["Bt"][k * nc:(k + 1) * nc].copy_(pinned["Bt"][k * nc:(k + 1) * nc], non_blocking=True)
+                        st["sB"][k * sb_chunk:(k + 1) * sb_chunk].copy_(
+                            pinned["sB"][k * sb_chunk:(k + 1) * sb_chunk], non_blocking=True)
                     ev = torch.cuda.Event()
                     ev.record(s_up)
                     if kind_c == "A":
@@ -953,54 +960,77 @@ def run_ours(args):
                     else:
                         blocks += [(i, k, ev) for i in have_a]
                         have_b.append(k)
+            if st["down"] is not None:
+                stream.wait_event(st["down"])  # the step before last's result has left this set's D
             done = []
+            Dd = st["D"]
             for i, j, ev in blocks:
                 stream.wait_event(ev)
-                lib.gemm_gather(ot, mc, nc, Kp, dA2[i * mc:], dB2[j * nc:], dsA2[i * sa_chunk:], dsB2[j * sb_chunk:],
-                                [D[i * mc:].data_ptr()], N, j * nc, rb, rb, ws_c, wsb_c, stream=stream)
+                lib.gemm_gather(ot, mc, nc, Kp, st["A"][i * mc:], st["Bt"][j * nc:], st["sA"][i * sa_chunk:],
+                                st["sB"][j * sb_chunk:], [Dd[i * mc:].data_ptr()], N, j * nc, rb, rb, ws_c, wsb_c,
+                                stream=stream)
                 ev = torch.cuda.Event()
                 ev.record(stream)
                 done.append((i, j, ev))
+            st["computed"] = done[-1][2]
+            Dh = st["Dh"]
             for i, j, ev in done:
                 s_down.wait_event(ev)
                 off = (i * mc * N + j * nc) * esz
-                err = memcpy2d(Dh.data_ptr() + off, N * esz, D.data_ptr() + off, N * esz, nc * esz, mc,
+                err = memcpy2d(Dh.data_ptr() + off, N * esz, Dd.data_ptr() + off, N * esz, nc * esz, mc,
                                CUDA_MEMCPY_D2H, s_down.cuda_stream)
                 if err != 0:
                     raise RuntimeError(f"cudaMemcpy2DAsync failed: {err}")
-            ev_end = torch.cuda.Event()
-            ev_end.record(s_down)
-            stream.wait_event(ev_end)
+            st["down"] = torch.cuda.Event()
+            st["down"].record(s_down)
 
-        e2e_steps = max(3, min(args.steps, 20))
+        def timed(n, pipelined):
+            """ms per step over n steps, from an event on the compute stream before the first
+            upload to one after the last result has landed in host memory."""
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            s_up.wait_event(e0)
+            for k in range(n):
+                e2e_step(sets[k % 2] if pipelined else sets[0])
+                if not pipelined:  # the next step starts once this one's result is in host memory
+                    s_up.wait_event(sets[0]["down"])
+            for st in sets:
+                if st["down"] is not None:
+                    stream.wait_event(st["down"])
+            e1.record(stream)
+            torch.cuda.synchronize()
+            return e0.elapsed_time(e1) / n
+
+        e2e_steps = max(4, min(args.steps, 20))
         D_dev = D.clone()  # the device-timed result, to compare the end-to-end output with
-        for _ in range(2):
-            e2e_step()
-        torch.cuda.synchronize()
+        timed(2, True)
         bits = torch.int32 if tdt == torch.float32 else torch.int16
-        e2e_same = float((Dh.to(dev).view(bits) == D_dev.view(bits)).float().mean().item())
+        e2e_same = min(float((st["Dh"].to(dev).view(bits) == D_dev.view(bits)).float().mean().item())
+                       for st in sets)
         del D_dev
         if world > 1:
             dist.barrier()
-        e0 = torch.cuda.Event(enable_timing=True)
-        e1 = torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
-        for _ in range(e2e_steps):
-            e2e_step()
-        e1.record(stream)
-        torch.cuda.synchronize()
-        e2e_ms = e0.elapsed_time(e1) / e2e_steps
+        serial_ms = timed(e2e_steps, False)
         if world > 1:
-            t = torch.tensor([e2e_ms], device=dev, dtype=torch.float64)
+            dist.barrier()
+        e2e_ms = timed(e2e_steps, True)
+        if world > 1:
+            t = torch.tensor([e2e_ms, serial_ms], device=dev, dtype=torch.float64)
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            e2e_ms = float(t.item())
+            e2e_ms, serial_ms = float(t[0].item()), float(t[1].item())
         e2e_value = flops_rank * world / (e2e_ms * 1e-3) / 1e12
         return {"value": e2e_value, "unit": "TFLOPS", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "ms_per_step": e2e_ms, "bitwise_equal_to_device_run": e2e_same,
+                "one_step_at_a_time": {"ms_per_step": serial_ms,
+                                       "value": flops_rank * world / (serial_ms * 1e-3) / 1e12,
+                                       "how": "each step's uploads start after the previous step's result "
+                                              "is in host memory"},
                 "path": f"pinned host -> H2D in {ra} row chunks of A and {rc} of B^T (interleaved, with their "
                         f"scales), overlapped with one C-ABI call (mxfp6_gemm_gather, one destination) per "
                         f"{mc}x{nc} block of D as soon as its chunks land, overlapped with a pitched D2H "
-                        f"copy per block"}
+                        f"copy per block; consecutive steps on alternate buffer sets, so one step's uploads "
+                        f"overlap the previous step's downloads"}
 
     e2e = None if args.no_e2e else e2e_leg()
 
@@ -1215,8 +1245,10 @@ def main():
                     help="also time the same GEMM with A in the reference's compact layout (loader warps, "
                          "library re-pad scratch, caller workspace)")
     ap.add_argument("--ref-seconds", type=float, default=10.0, help="target CPU seconds per reference sample")
-    ap.add_argument("--e2e-cols", type=int, default=4,
+    ap.add_argument("--e2e-cols", type=int, default=2,
                     help="column chunks of B and D in the end-to-end pipeline (1 = row chunks only)")
+    ap.add_argument("--e2e-rows", type=int, default=E2E_ROW_CHUNKS,
+                    help="row chunks of A and D in the end-to-end pipeline (1 = column chunks only)")
     ap.add_argument("--strong", action="store_true",
                     help="split the config's N over the ranks (strong scaling) instead of N per rank")
     ap.add_argument("--shard-of", type=int, default=1,
