@@ -73,7 +73,11 @@ E2E_ROW_CHUNKS = 8  # default row chunks of A (and of D) in the end-to-end step
 CUDA_MEMCPY_D2H = 2
 # DRAM bytes (read + write) per launch of the dominant kernel, from one ncu capture of this
 # bench's own command (profiles/gemm_mxfp6_sm100_pair_cfg2.md); None where not captured yet.
-NCU_TRAFFIC_BYTES = {"cfg2": 163_303_936 + 112_370_944}
+# DRAM bytes (read + write) of the dominant kernel per launch, from one ncu capture each (the
+# summaries under profiles/ give the commands): cfg2 and cfg5 with the current kernel, cfg3 (the
+# banded split's pair kernel, without the reduce) and cfg4 with the same tiling and schedule.
+NCU_TRAFFIC_BYTES = {"cfg2": 166_301_440 + 112_045_824, "cfg3": 292_300_000 + 10_100_000,
+                     "cfg4": 198_600_000 + 30_300_000, "cfg5": 251_785_216 + 236_046_592}
 NOMINAL_FP6_TFLOPS = 4500.0  # B200 dense FP8/FP6 tensor rate, nominal (no sparsity)
 SEED_A, SEED_B = 1000, 2000  # operand seeds (B: plus the rank of its shard)
 
@@ -540,6 +544,8 @@ def per_config_leg(lib, torch, dev, stream, flush, steps, warmup, skip):
                  "route": lib.route(ot, M, N, Kp), "ms": ms, "best_ms": min(per), "steps": steps,
                  "error": err, "device_status": status}
         entry.update(roofline_fields(M, N, K, Kp, D.element_size(), ms, wsb))
+        if name in NCU_TRAFFIC_BYTES:
+            entry["traffic"] = NCU_TRAFFIC_BYTES[name]  # dominant kernel's DRAM bytes per launch (ncu)
         if name == "cfg1":
             entry["back_to_back"] = back_to_back_per_call(torch, call_on, stream)
             entry["back_to_back"].update(cpp_cfg1_per_call())
@@ -798,6 +804,7 @@ def strong_leg(lib, torch, dist, dev, stream, flush, rank, world, steps, warmup,
                   if k not in ("tflops",)})
     if world == 1:
         D_full = D_r
+        entry["traffic"] = NCU_TRAFFIC_BYTES["cfg5"]  # the pair kernel's DRAM bytes per launch (ncu)
         entry["one_gpu"] = {"ms": ms, "tflops": total}
         entry["efficiency_vs_one_gpu"] = 1.0
     else:
