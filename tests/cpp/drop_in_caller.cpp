@@ -14,6 +14,8 @@
 //   drop_in_caller time   per-call time of the launch-bound BASELINE config 1 (256x256x512, FP32
 //                         out) timed the reference's way: 8 warm-ups, then 20 back-to-back gemm()
 //                         calls on the legacy default stream between two events, best of 4
+//   drop_in_caller time M N K OUT   the same for one shape (OUT F32, F16 or BF16; K zero-padded
+//                         to kpad(K) as the reference's harness pads it)
 // Exit status 0 on success; each failure prints one line.
 #include <cuda_runtime.h>
 
@@ -215,13 +217,18 @@ void run_case(const Shape& s, OutType ot, uint32_t seed) {
 
 // BASELINE config 1 through the public C++ API, timed as the reference times its launch-bound
 // floor (tests/test_gemm.cpp:32-52): host enqueue and device time of back-to-back calls.
-void time_cfg1() {
-    const int M = 256, N = 256, K = 512, Kp = kpad(K);
+// Per-call time of M x N x K (K zero-padded to kpad(K), as the reference's harness pads it) timed
+// the reference's way: 8 warm-ups, then 20 back-to-back gemm() calls on the legacy default stream
+// between two events, best of 4. Operands are N(0, 1) rows quantised with the public helpers.
+void time_shape(int M, int N, int K, OutType ot, const std::string& label) {
+    const int Kp = kpad(K);
     std::mt19937 rng(5);
     std::normal_distribution<float> nd(0.0f, 1.0f);
-    std::vector<float> A((size_t)M * Kp), B((size_t)Kp * N);
-    for (float& v : A) v = nd(rng);
-    for (float& v : B) v = 0.05f * nd(rng);
+    std::vector<float> A((size_t)M * Kp, 0.0f), B((size_t)Kp * N, 0.0f);
+    for (int r = 0; r < M; r++)
+        for (int k = 0; k < K; k++) A[(size_t)r * Kp + k] = nd(rng);
+    for (int k = 0; k < K; k++)
+        for (int c = 0; c < N; c++) B[(size_t)k * N + c] = 0.05f * nd(rng);
     QuantizedMatrix Aq = quantize_to_mxfp6(A.data(), M, Kp);
     QuantizedMatrix Bq = preprocess_B(B.data(), Kp, N);
     PreshuffledB Bsh = preshuffle_B(Bq);
@@ -229,20 +236,21 @@ void time_cfg1() {
     TiledScale sA = tile_scale(preprocess_scale(Aq.scales.data(), M, Kp), tc.MPW, K_TILE / 64);
     TiledScale sB = tile_scale(preprocess_scale(Bq.scales.data(), N, Kp), tc.NPW, K_TILE / 64);
     const size_t wsb = gemm_workspace_size(M, N, Kp);
+    const size_t esize = ot == OutType::F32 ? 4 : 2;
     void *dA, *dB, *dD, *ws = nullptr;
     uint8_t *dsA, *dsB;
     CUDA_OK(cudaMalloc(&dA, Aq.packed_data.size()));
     CUDA_OK(cudaMalloc(&dB, Bsh.data.size()));
     CUDA_OK(cudaMalloc(&dsA, sA.data.size()));
     CUDA_OK(cudaMalloc(&dsB, sB.data.size()));
-    CUDA_OK(cudaMalloc(&dD, (size_t)M * N * 4));
+    CUDA_OK(cudaMalloc(&dD, (size_t)M * N * esize));
     if (wsb) CUDA_OK(cudaMalloc(&ws, wsb));
     CUDA_OK(cudaMemcpy(dA, Aq.packed_data.data(), Aq.packed_data.size(), cudaMemcpyHostToDevice));
     CUDA_OK(cudaMemcpy(dB, Bsh.data.data(), Bsh.data.size(), cudaMemcpyHostToDevice));
     CUDA_OK(cudaMemcpy(dsA, sA.data.data(), sA.data.size(), cudaMemcpyHostToDevice));
     CUDA_OK(cudaMemcpy(dsB, sB.data.data(), sB.data.size(), cudaMemcpyHostToDevice));
     auto call = [&] {
-        gemm(OutType::F32, M, N, Kp, dA, dB, dsA, dsB, dD, Aq.packed_row_bytes, Bq.packed_row_bytes, ws, wsb);
+        gemm(ot, M, N, Kp, dA, dB, dsA, dsB, dD, Aq.packed_row_bytes, Bq.packed_row_bytes, ws, wsb);
     };
     for (int i = 0; i < 8; i++) call();
     CUDA_OK(cudaDeviceSynchronize());
@@ -259,9 +267,9 @@ void time_cfg1() {
         CUDA_OK(cudaEventElapsedTime(&ms, e0, e1));
         if (ms < best) best = ms;
     }
-    if (mxfp6_last_error() != MXFP6_OK || mxfp6_device_status() != 0) fail("cfg1 timing calls reported an error");
-    std::printf("cfg1 back-to-back from C++: %.3f us per call (%s, 20 calls, best of 4)\n", best * 1000.0f / 20,
-                "256x256x512 FP32 out");
+    if (mxfp6_last_error() != MXFP6_OK || mxfp6_device_status() != 0) fail(label + " timing calls reported an error");
+    std::printf("%s back-to-back from C++: %.3f us per call (%dx%dx%d %s out, 20 calls, best of 4)\n", label.c_str(),
+                best * 1000.0f / 20, M, N, K, ot == OutType::F32 ? "FP32" : ot == OutType::F16 ? "FP16" : "BF16");
     cudaEventDestroy(e0);
     cudaEventDestroy(e1);
     cudaFree(dA);
@@ -298,9 +306,18 @@ int main(int argc, char** argv) {
         host_checks();
         gpu_checks();
     } else if (mode == "time") {
-        time_cfg1();
+        if (argc == 2) {
+            time_shape(256, 256, 512, OutType::F32, "cfg1");
+        } else if (argc == 6) {
+            const std::string o = argv[5];
+            const OutType ot = o == "F32" ? OutType::F32 : o == "BF16" ? OutType::BF16 : OutType::F16;
+            time_shape(std::atoi(argv[2]), std::atoi(argv[3]), std::atoi(argv[4]), ot, "shape");
+        } else {
+            std::printf("usage: %s time [M N K F32|F16|BF16]\n", argv[0]);
+            return 2;
+        }
     } else {
-        std::printf("usage: %s host|gpu|time\n", argv[0]);
+        std::printf("usage: %s host|gpu|time [M N K OUT]\n", argv[0]);
         return 2;
     }
     std::printf("%s: %d failure(s)\n", mode.c_str(), g_failures);
