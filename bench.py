@@ -18,7 +18,11 @@ Every line also carries
                 equal the unsplit D bit for bit, and the optional D all-gather (NCCL, and the
                 fused epilogue gather over NVLink peer stores) at N>1;
   "per_config"  (N=1) device-timed TFLOPS, route and roofline fractions of BASELINE configs 1, 3,
-                4 and 5, plus the device quantiser and the reference-layout import on config 5.
+                4 and 5, plus the device quantiser and the reference-layout import on config 5;
+  "ref_sweep"   (N=1) the reference's headline shape table (M=2048, FP16 out, its 36 measured
+                (N, K) rows) timed its way, each row against the reference's published MI350X
+                latency, with a count-weighted and a geometric-mean speed-up (--ref-sweep prints
+                it alone, one line per shape; --no-ref-sweep skips it).
 
 Timing: W untimed warm-up steps; then exactly K steps between a barrier + synchronize on each
 side; before every timed step a 256 MiB buffer is written to flush the 126 MB L2, and each
@@ -77,7 +81,7 @@ CUDA_MEMCPY_D2H = 2
 # DRAM bytes (read + write) of the dominant kernel per launch, from one ncu capture each (the
 # summaries under profiles/ give the commands): cfg2 and cfg5 with the current kernel, cfg3 (the
 # banded split's pair kernel, without the reduce) and cfg4 with the same tiling and schedule.
-NCU_TRAFFIC_BYTES = {"cfg2": 166_301_440 + 112_045_824, "cfg3": 292_300_000 + 10_100_000,
+NCU_TRAFFIC_BYTES = {"cfg2": 163_994_112 + 112_266_240, "cfg3": 292_300_000 + 10_100_000,
                      "cfg4": 198_600_000 + 30_300_000, "cfg5": 251_785_216 + 236_046_592}
 NOMINAL_FP6_TFLOPS = 4500.0  # B200 dense FP8/FP6 tensor rate, nominal (no sparsity)
 SEED_A, SEED_B = 1000, 2000  # operand seeds (B: plus the rank of its shard)
@@ -1142,6 +1146,14 @@ def run_ours(args):
             per_config["cfg5"] = {k: v for k, v in strong.items()
                                   if k not in ("one_gpu", "efficiency_vs_one_gpu", "N_total", "N_per_gpu")}
             per_config["cfg5"]["N"] = CONFIGS["cfg5"][1]
+    # ---- the reference's headline shape table, timed its way, against its published latencies ----
+    ref_sweep = None
+    if world == 1 and not args.no_ref_sweep:
+        rows, ref_sweep = ref_sweep_leg(lib, torch, dev, stream, flush, quiet=True)
+        ref_sweep["by_shape"] = [{"shape": r["shape"], "route": r["route"], "ms": r["ms"],
+                                  "reference_mi350x_ms": r["reference_mi350x_ms"],
+                                  "speedup": r["speedup_vs_reference"], "timed_from": "C++" if "ms_cpp" in r else "Python"}
+                                 for r in rows]
 
     # ---- CPU baseline (rank 0, N=1 only) ----
     cpu = None
@@ -1177,6 +1189,8 @@ def run_ours(args):
             line["strong"] = strong
         if per_config:
             line["per_config"] = per_config
+        if ref_sweep:
+            line["ref_sweep"] = ref_sweep
         if compact:
             line["compact_a"] = compact
         if as_ref:
@@ -1409,6 +1423,8 @@ def main():
                     help="on one GPU, run the N shard one rank of this many holds (strong scaling)")
     ap.add_argument("--import-only", action="store_true",
                     help="only time the device import of the config's B from the reference's layout")
+    ap.add_argument("--no-ref-sweep", action="store_true",
+                    help="skip the reference's headline shape table in the N=1 line")
     ap.add_argument("--ref-sweep", action="store_true",
                     help="time the reference's headline shape sweep (M=2048, FP16) and compare with its "
                          "published MI350X latencies; one JSON line per shape and a summary")
