@@ -443,7 +443,7 @@ __global__ void __launch_bounds__(threads_for(AMODE), 1)
                 if (col0 + c >= p.N) break;  // masked half tile (uniform across the warp)
                 uint32_t r[32];
                 sm100::tmem_ld_32x32b_x32(t_row + (uint32_t)c, r);
-                sm100::tmem_ld_wait();
+                sm100::tmem_ld_wait(r);
                 if (row < p.M) {
                     if constexpr (PARTIAL) {
                         float* dst = p.ws + ((size_t)tc.split * p.M + row) * p.N + col0 + c;

@@ -553,7 +553,7 @@ __global__ void __launch_bounds__(threads_for(AMODE), 1)
                 const uint32_t tcol = (b ? C::BUF1_COL : 0) + 32 * c;
                 uint32_t r[32];
                 sm100::tmem_ld_32x32b_x32(t_lane + tcol, r);
-                sm100::tmem_ld_wait();
+                sm100::tmem_ld_wait(r);
                 if (j == 0) {
                     sm100::tc_fence_before();
                     __syncwarp();
