@@ -70,3 +70,17 @@ def test_reference_arm_maps_no_product_library(tmp_path):
     ref_line, probe = lines[0], lines[-1]
     assert probe == {"pkg": False, "so": False}
     assert ref_line["impl"] == "reference" and ref_line["config"] == __import__("bench").bench_config("cfg1", 1, 1)
+
+
+def test_reference_sweep_table():
+    """The reference's headline table as the sweep leg carries it (benchmark_results.md:23-74 of
+    eeezio/mxfp6-gemm, its 36 measured rows): M = 2048, unique (N, K), every N a multiple of 128
+    (a shape this library runs), and the count-weighted total of the published MI350X latencies
+    that the leg's summary compares against."""
+    import bench
+    rows = bench.REF_SWEEP
+    assert bench.REF_SWEEP_M == 2048 and len(rows) == 36
+    assert len({(n, k) for n, k, _, _ in rows}) == 36
+    assert all(n % 128 == 0 and k > 0 and c > 0 and ms > 0 for n, k, c, ms in rows)
+    assert sum(c * ms for _, _, c, ms in rows) == pytest.approx(10.135534, abs=1e-6)
+    assert sum(c for _, _, c, _ in rows) == 285
