@@ -134,7 +134,11 @@ inline double route_cost_us(int M, int N, int Kp, int MT, int NT, int S, int sms
         t_fixed = 0.3;
         per_unit = 1;
     } else {
-        t_slab = 0.24;
+        // about 0.9 of the pair's rate per slab at full occupancy (0.38-0.42 us a slab back to
+        // back on 64-128 CTAs). At 0.24 the model kept deep-K shapes on one 128x128 wave that
+        // run faster split: 2048x1024x12288 39.1 us against 31.9 us as a 2-way split on the pair,
+        // 2048x256x4096 15.0 against 12.5 us split 3 ways (back to back, B200).
+        t_slab = 0.27;
         t_tile = 0.6;
         t_fixed = 0.0;
         per_unit = 1;
