@@ -157,6 +157,16 @@ def test_route_examples(lib):
         assert lib.choose_tile(*shape).MT == 256, shape
 
 
+@pytest.mark.parametrize("M,N,K,MT,NT,splits", [(2048, 1024, 12288, 256, 256, 2), (2048, 256, 4096, 128, 128, 3),
+                                                 (2048, 256, 16128, 128, 256, 6), (2048, 512, 6144, 128, 128, 2)])
+def test_deep_k_one_wave_shapes_split(lib, M, N, K, MT, NT, splits):
+    """One wave of 128x128 tiles with a deep K runs faster split (measured back to back on B200:
+    2048x1024x12288 39.1 us on one 128x128 wave, 31.9 us as a 2-way split on the CTA pair)."""
+    r = lib.route(lib.OutType.F16, M, N, lib.kpad(K))
+    assert (r["MT"], r["NT"], r["splits"]) == (MT, NT, splits), r
+    assert lib.gemm_workspace_size(M, N, lib.kpad(K), lib.OutType.F16) == splits * M * N * 4
+
+
 @pytest.mark.parametrize("M,N,K", [(128, 128, 128), (256, 256, 512), (512, 512, 1024), (512, 256, 2048),
                                    (1024, 2048, 8192)])
 def test_small_shapes_take_the_single_cta_kernel_unsplit(lib, M, N, K):
