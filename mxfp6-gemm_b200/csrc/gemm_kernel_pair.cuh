@@ -105,6 +105,9 @@ __device__ __forceinline__ int band_short_begin(const Params& p, int j) {
     return p.band_L * p.band_a + (int)((long long)ks * j / p.band_n);
 }
 
+// FULL: the launch may run a stream-K tail (hand-offs between pairs). A launch without one is
+// instantiated without that code (FULL = false).
+template <bool FULL>
 __device__ __forceinline__ PairWork pair_work(const Params& p, int pair, int npairs) {
     PairWork w;
     if (p.band_L > 0) {
@@ -120,13 +123,13 @@ __device__ __forceinline__ PairWork pair_work(const Params& p, int pair, int npa
         return w;
     }
     const int tiles = p.m_blocks * p.n_blocks * p.splits;
-    const int rr = p.sk_total > 0 ? p.sk_first : tiles;
+    const int rr = FULL && p.sk_total > 0 ? p.sk_first : tiles;
     w.n_whole = pair < rr ? (rr - pair + npairs - 1) / npairs : 0;
     w.n = w.n_whole;
     w.lo = w.hi = 0;
     w.hand_off = w.take_over = false;
     w.f0 = w.f1 = 0;
-    if (p.sk_total > 0) {
+    if (FULL && p.sk_total > 0) {
         const long long ks = p.k_slabs;
         w.lo = p.sk_total * pair / npairs;
         w.hi = p.sk_total * (pair + 1) / npairs;
@@ -139,6 +142,7 @@ __device__ __forceinline__ PairWork pair_work(const Params& p, int pair, int npa
     return w;
 }
 
+template <bool FULL>
 __device__ __forceinline__ PairUnit pair_unit(const Params& p, const PairWork& w, int pair, int npairs, int i) {
     PairUnit u;
     u.mode = UNIT_WHOLE;
@@ -160,7 +164,7 @@ __device__ __forceinline__ PairUnit pair_unit(const Params& p, const PairWork& w
         }
         return u;
     }
-    if (w.hand_off) {
+    if (FULL && w.hand_off) {
         if (i == 0) {
             u.tc = decode_tile(p.sk_first + (int)(w.hi / ks), p);
             u.tc.kb_begin = 0;
@@ -191,7 +195,10 @@ __device__ __forceinline__ PairUnit pair_unit(const Params& p, const PairWork& w
 // AMODE (compact_a.cuh): A_TMA loads A with the 16U6 tensor load; A_CPASYNC adds four
 // loader warps per CTA that build the A image from p.a_ptr, and whose arrivals join the leader's
 // full barrier.
-template <typename OutT, bool PARTIAL, int AMODE = A_TMA>
+// FULL (non-partial launches): the epilogue may hand accumulators between pairs (stream-K tail) or
+// write several destinations (gather). Launches that do neither use the FULL = false instantiation,
+// which leaves that code out: measured 2-11% faster on such shapes.
+template <typename OutT, bool PARTIAL, int AMODE = A_TMA, bool FULL = true>
 __global__ void __launch_bounds__(threads_for(AMODE), 1)
     gemm_mxfp6_sm100_pair(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                           const __grid_constant__ CUtensorMap tmSA, const __grid_constant__ CUtensorMap tmSB,
@@ -276,7 +283,8 @@ __global__ void __launch_bounds__(threads_for(AMODE), 1)
 
     const int cluster_id = blockIdx.x >> 1;
     const int num_clusters = gridDim.x >> 1;
-    const PairWork work = pair_work(p, cluster_id, num_clusters);
+    constexpr bool XF = FULL && !PARTIAL;  // stream-K hand-offs or several destinations possible
+    const PairWork work = pair_work<XF>(p, cluster_id, num_clusters);
     // Abort bookkeeping, read after the roles have finished (see the end of the kernel): the
     // producer's last load per stage and its phase parity, and whether any MMA was issued.
     uint32_t issued_mask = 0, issued_phase = 0;
@@ -292,7 +300,7 @@ __global__ void __launch_bounds__(threads_for(AMODE), 1)
             constexpr uint32_t tx = 2u * ((COMPACT ? 0u : (uint32_t)A_TMA_BYTES) + 128u * (BK * 3 / 4) +
                                           (uint32_t)C::SF_STAGE);
             for (int ui = 0; ui < work.n && ok; ui++) {
-                const PairUnit u = pair_unit(p, work, cluster_id, num_clusters, ui);
+                const PairUnit u = pair_unit<XF>(p, work, cluster_id, num_clusters, ui);
                 const TileCoord& tc = u.tc;
                 const int a_row = tc.mb * C::BM + 128 * (int)rank;
                 const int b_row = tc.nb * C::BN + 128 * (int)rank;
@@ -338,7 +346,7 @@ __global__ void __launch_bounds__(threads_for(AMODE), 1)
             const uint32_t sfb_t = tmem_base + C::TMEM_SFB;
             int local = 0;  // units this pair has computed: selects the accumulator buffer
             for (int ui = 0; ui < work.n && ok; ui++) {
-                const PairUnit u = pair_unit(p, work, cluster_id, num_clusters, ui);
+                const PairUnit u = pair_unit<XF>(p, work, cluster_id, num_clusters, ui);
                 const TileCoord& tc = u.tc;
                 const int b = local & 1;
                 const uint32_t d_taddr = tmem_base + (b ? C::BUF1_COL : 0);
@@ -352,13 +360,13 @@ __global__ void __launch_bounds__(threads_for(AMODE), 1)
                     break;
                 }
                 // A taken-over tile continues the accumulator the epilogue loaded (one per launch)
-                if (u.mode == UNIT_TAKE_OVER && !sm100::wait_parity_bounded(fill_bar, 0, abort_flag, p.wait_budget)) {
+                if (XF && u.mode == UNIT_TAKE_OVER && !sm100::wait_parity_bounded(fill_bar, 0, abort_flag, p.wait_budget)) {
                     if (!*abort_flag) raise(0x2u);
                     *abort_flag = 1;
                     ok = false;
                     break;
                 }
-                const uint32_t acc0 = u.mode == UNIT_TAKE_OVER ? 1u : 0u;
+                const uint32_t acc0 = XF && u.mode == UNIT_TAKE_OVER ? 1u : 0u;
                 sm100::tc_fence_after();
                 // The issuing thread keeps the tensor pipe's short queue fed: it polls the next
                 // slab's barrier without blocking right after issuing the current one, and
@@ -403,7 +411,7 @@ __global__ void __launch_bounds__(threads_for(AMODE), 1)
             uint32_t phase = 0;
             bool ok = true;
             for (int ui = 0; ui < work.n && ok; ui++) {
-                const TileCoord tc = pair_unit(p, work, cluster_id, num_clusters, ui).tc;
+                const TileCoord tc = pair_unit<XF>(p, work, cluster_id, num_clusters, ui).tc;
                 for (int i = 0; i < tc.kb_count; i++) {
                     if (!sm100::wait_parity_bounded(full_bar(stage), phase, abort_flag, p.wait_budget)) {
                         if (!*abort_flag) raise(0x1u);
@@ -429,7 +437,7 @@ __global__ void __launch_bounds__(threads_for(AMODE), 1)
         uint32_t phase = 0;
         bool ok = true;
         for (int ui = 0; ui < work.n && ok; ui++) {
-            const TileCoord tc = pair_unit(p, work, cluster_id, num_clusters, ui).tc;
+            const TileCoord tc = pair_unit<XF>(p, work, cluster_id, num_clusters, ui).tc;
             const int a_row = tc.mb * C::BM + 128 * (int)rank;
             for (int i = 0; i < tc.kb_count; i++) {
                 int got = 1;
@@ -507,7 +515,7 @@ __global__ void __launch_bounds__(threads_for(AMODE), 1)
         };
         int local = 0;  // units this pair has computed: selects the accumulator buffer
         for (int ui = 0; ui < work.n; ui++) {
-            const PairUnit u = pair_unit(p, work, cluster_id, num_clusters, ui);
+            const PairUnit u = pair_unit<XF>(p, work, cluster_id, num_clusters, ui);
             const TileCoord& tc = u.tc;
             const int b = local & 1;
             // The unit after this one, when it takes over a tile, gets its accumulator loaded into
@@ -515,16 +523,16 @@ __global__ void __launch_bounds__(threads_for(AMODE), 1)
             // other buffer's previous unit is drained), the shared chunk once this unit's epilogue
             // has read it. After a hand-off, the whole load waits until this pair's own flag is out
             // (the next pair may be waiting for it).
-            const bool next_takes_over = !PARTIAL && ui + 1 < work.n &&
-                                         pair_unit(p, work, cluster_id, num_clusters, ui + 1).mode == UNIT_TAKE_OVER;
-            const bool hand_off = !PARTIAL && u.mode == UNIT_HAND_OFF;
+            const bool next_takes_over = XF && ui + 1 < work.n &&
+                                         pair_unit<XF>(p, work, cluster_id, num_clusters, ui + 1).mode == UNIT_TAKE_OVER;
+            const bool hand_off = XF && u.mode == UNIT_HAND_OFF;
             const bool early = next_takes_over && !hand_off;
-            if (early && !take_over(pair_unit(p, work, cluster_id, num_clusters, ui + 1), b ^ 1, FILL_REST)) {
+            if (early && !take_over(pair_unit<XF>(p, work, cluster_id, num_clusters, ui + 1), b ^ 1, FILL_REST)) {
                 if (lane == 0 && !*abort_flag) raise(0x4u);
                 *abort_flag = 1;
                 break;
             }
-            if (!PARTIAL && u.mode == UNIT_TAKE_OVER && local == 0 && !take_over(u, b, FILL_ALL)) {
+            if (XF && u.mode == UNIT_TAKE_OVER && local == 0 && !take_over(u, b, FILL_ALL)) {
                 if (lane == 0 && !*abort_flag) raise(0x4u);
                 *abort_flag = 1;
                 break;
@@ -533,7 +541,7 @@ __global__ void __launch_bounds__(threads_for(AMODE), 1)
             // release of the shared chunk, the MMA thread waits and the tensor pipe idles.
             const int row = tc.mb * C::BM + tile_row;
             const int col0 = tc.nb * C::BN;
-            const bool regroup = !PARTIAL && !hand_off && p.dst.n > 1;
+            const bool regroup = XF && !hand_off && p.dst.n > 1;
             // The whole warp waits (a suspended wait takes no issue slots), so it is still converged
             // when the accumulator completes. Measured on B200: 1.7% on cfg2 against one polling
             // lane and a shuffle.
@@ -558,7 +566,7 @@ __global__ void __launch_bounds__(threads_for(AMODE), 1)
                     sm100::tc_fence_before();
                     __syncwarp();
                     if (lane == 0) sm100::mbar_arrive_remote(leader_ovl_free);
-                    if (early) take_over(pair_unit(p, work, cluster_id, num_clusters, ui + 1), b ^ 1, FILL_SHARED);
+                    if (early) take_over(pair_unit<XF>(p, work, cluster_id, num_clusters, ui + 1), b ^ 1, FILL_SHARED);
                 }
                 const int col = col0 + 32 * c;
                 if (hand_off) {
@@ -616,7 +624,7 @@ __global__ void __launch_bounds__(threads_for(AMODE), 1)
                     }
                 }
                 __syncwarp();
-                if (next_takes_over && !take_over(pair_unit(p, work, cluster_id, num_clusters, ui + 1), b ^ 1, FILL_ALL)) {
+                if (next_takes_over && !take_over(pair_unit<XF>(p, work, cluster_id, num_clusters, ui + 1), b ^ 1, FILL_ALL)) {
                     if (lane == 0 && !*abort_flag) raise(0x4u);
                     *abort_flag = 1;
                     break;
