@@ -425,10 +425,11 @@ bool launch_pair(int M, int N, int Kp, const void* dA, const void* dB, const uin
                  const kern::DstList& dl, float* ws, int A_row_bytes, int B_row_bytes, int splits, void* sk_area,
                  cudaStream_t stream, const BandedSplit* band = nullptr) {
     using C = kern::PairConfig<AMODE>;
-    // the kernel without stream-K hand-offs and multi-destination stores, and the one with them
-    // (the same instantiation in partial mode, which has neither)
-    auto kernel_lean = kern::gemm_mxfp6_sm100_pair<OutT, PARTIAL, AMODE, false>;
-    auto kernel_full = kern::gemm_mxfp6_sm100_pair<OutT, PARTIAL, AMODE, !PARTIAL>;
+    // the kernel without stream-K hand-offs and multi-destination stores, with hand-offs, and with
+    // both (one instantiation in partial mode, which has neither)
+    auto kernel_lean = kern::gemm_mxfp6_sm100_pair<OutT, PARTIAL, AMODE, kern::EPI_LEAN>;
+    auto kernel_sk = kern::gemm_mxfp6_sm100_pair<OutT, PARTIAL, AMODE, PARTIAL ? kern::EPI_LEAN : kern::EPI_STREAM_K>;
+    auto kernel_all = kern::gemm_mxfp6_sm100_pair<OutT, PARTIAL, AMODE, PARTIAL ? kern::EPI_LEAN : kern::EPI_ALL>;
     static std::once_flag attr_once[kMaxDevices];
     const int dev = current_device();
     if (dev < 0 || dev >= kMaxDevices) {
@@ -437,9 +438,9 @@ bool launch_pair(int M, int N, int Kp, const void* dA, const void* dB, const uin
     }
     cudaError_t attr_err = cudaSuccess;
     std::call_once(attr_once[dev], [&] {
-        attr_err = cudaFuncSetAttribute(kernel_lean, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
-        if (attr_err == cudaSuccess)
-            attr_err = cudaFuncSetAttribute(kernel_full, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
+        for (auto k : {kernel_lean, kernel_sk, kernel_all})
+            if (attr_err == cudaSuccess)
+                attr_err = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
     });
     if (attr_err != cudaSuccess) {
         set_error(MXFP6_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(attr_err));
@@ -504,8 +505,8 @@ bool launch_pair(int M, int N, int Kp, const void* dA, const void* dB, const uin
     set_pdl(attr[1]);
     cfg.attrs = attr;
     cfg.numAttrs = 2;
-    const bool full = !PARTIAL && (p.sk_total > 0 || dl.n > 1);
-    cudaError_t e = cudaLaunchKernelEx(&cfg, full ? kernel_full : kernel_lean, tmA, tmB, tmSA, tmSB, p);
+    const auto kernel = PARTIAL ? kernel_lean : dl.n > 1 ? kernel_all : p.sk_total > 0 ? kernel_sk : kernel_lean;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, tmA, tmB, tmSA, tmSB, p);
     if (e == cudaSuccess) e = cudaGetLastError();
     if (e != cudaSuccess) {
         set_error(MXFP6_ERR_CUDA, "pair GEMM launch failed: %s", cudaGetErrorString(e));

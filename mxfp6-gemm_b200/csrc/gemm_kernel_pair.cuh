@@ -105,9 +105,9 @@ __device__ __forceinline__ int band_short_begin(const Params& p, int j) {
     return p.band_L * p.band_a + (int)((long long)ks * j / p.band_n);
 }
 
-// FULL: the launch may run a stream-K tail (hand-offs between pairs). A launch without one is
-// instantiated without that code (FULL = false).
-template <bool FULL>
+// SK: the launch may run a stream-K tail (hand-offs between pairs). A launch without one is
+// instantiated without that code (SK = false).
+template <bool SK>
 __device__ __forceinline__ PairWork pair_work(const Params& p, int pair, int npairs) {
     PairWork w;
     if (p.band_L > 0) {
@@ -123,13 +123,13 @@ __device__ __forceinline__ PairWork pair_work(const Params& p, int pair, int npa
         return w;
     }
     const int tiles = p.m_blocks * p.n_blocks * p.splits;
-    const int rr = FULL && p.sk_total > 0 ? p.sk_first : tiles;
+    const int rr = SK && p.sk_total > 0 ? p.sk_first : tiles;
     w.n_whole = pair < rr ? (rr - pair + npairs - 1) / npairs : 0;
     w.n = w.n_whole;
     w.lo = w.hi = 0;
     w.hand_off = w.take_over = false;
     w.f0 = w.f1 = 0;
-    if (FULL && p.sk_total > 0) {
+    if (SK && p.sk_total > 0) {
         const long long ks = p.k_slabs;
         w.lo = p.sk_total * pair / npairs;
         w.hi = p.sk_total * (pair + 1) / npairs;
@@ -142,7 +142,7 @@ __device__ __forceinline__ PairWork pair_work(const Params& p, int pair, int npa
     return w;
 }
 
-template <bool FULL>
+template <bool SK>
 __device__ __forceinline__ PairUnit pair_unit(const Params& p, const PairWork& w, int pair, int npairs, int i) {
     PairUnit u;
     u.mode = UNIT_WHOLE;
@@ -164,7 +164,7 @@ __device__ __forceinline__ PairUnit pair_unit(const Params& p, const PairWork& w
         }
         return u;
     }
-    if (FULL && w.hand_off) {
+    if (SK && w.hand_off) {
         if (i == 0) {
             u.tc = decode_tile(p.sk_first + (int)(w.hi / ks), p);
             u.tc.kb_begin = 0;
@@ -195,10 +195,12 @@ __device__ __forceinline__ PairUnit pair_unit(const Params& p, const PairWork& w
 // AMODE (compact_a.cuh): A_TMA loads A with the 16U6 tensor load; A_CPASYNC adds four
 // loader warps per CTA that build the A image from p.a_ptr, and whose arrivals join the leader's
 // full barrier.
-// FULL (non-partial launches): the epilogue may hand accumulators between pairs (stream-K tail) or
-// write several destinations (gather). Launches that do neither use the FULL = false instantiation,
-// which leaves that code out: measured 2-11% faster on such shapes.
-template <typename OutT, bool PARTIAL, int AMODE = A_TMA, bool FULL = true>
+// EPI (non-partial launches): which optional epilogue paths the instantiation carries. EPI_LEAN
+// has neither; EPI_STREAM_K adds the stream-K tail's hand-offs; EPI_ALL also writes several
+// destinations (gather). A launch uses the smallest that covers it: the unused code measured
+// 2-11% slower on shapes that never ran it.
+constexpr int EPI_LEAN = 0, EPI_STREAM_K = 1, EPI_ALL = 2;
+template <typename OutT, bool PARTIAL, int AMODE = A_TMA, int EPI = EPI_ALL>
 __global__ void __launch_bounds__(threads_for(AMODE), 1)
     gemm_mxfp6_sm100_pair(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                           const __grid_constant__ CUtensorMap tmSA, const __grid_constant__ CUtensorMap tmSB,
@@ -283,7 +285,8 @@ __global__ void __launch_bounds__(threads_for(AMODE), 1)
 
     const int cluster_id = blockIdx.x >> 1;
     const int num_clusters = gridDim.x >> 1;
-    constexpr bool XF = FULL && !PARTIAL;  // stream-K hand-offs or several destinations possible
+    constexpr bool XF = EPI >= EPI_STREAM_K && !PARTIAL;  // stream-K hand-offs possible
+    constexpr bool XG = EPI == EPI_ALL && !PARTIAL;        // several destinations possible
     const PairWork work = pair_work<XF>(p, cluster_id, num_clusters);
     // Abort bookkeeping, read after the roles have finished (see the end of the kernel): the
     // producer's last load per stage and its phase parity, and whether any MMA was issued.
@@ -541,7 +544,7 @@ __global__ void __launch_bounds__(threads_for(AMODE), 1)
             // release of the shared chunk, the MMA thread waits and the tensor pipe idles.
             const int row = tc.mb * C::BM + tile_row;
             const int col0 = tc.nb * C::BN;
-            const bool regroup = XF && !hand_off && p.dst.n > 1;
+            const bool regroup = XG && !hand_off && p.dst.n > 1;
             // The whole warp waits (a suspended wait takes no issue slots), so it is still converged
             // when the accumulator completes. Measured on B200: 1.7% on cfg2 against one polling
             // lane and a shuffle.
